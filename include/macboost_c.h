@@ -1,0 +1,147 @@
+/*
+ * macboost_c.h -- C ABI of the B200 batch-inference engine for MacBoost models.
+ *
+ * libmacboostc.so exports the inference subset of MacBoost's own C ABI
+ * (Sources/MacBoostC/CAPI.swift) with the same names, argument meanings and
+ * error behaviour, so MacBoost's Python ctypes bridge (python/macboost/_core.py)
+ * and Swift callers bind to it unchanged, plus additive entry points for
+ * output kinds, device lists, row-major input and device-resident buffers.
+ *
+ * Conventions (as in the reference):
+ *  - a model handle is an opaque pointer from macboost_load, released with
+ *    macboost_free;
+ *  - matrices are float32; `x` is feature-major, x[f * rows + i], unless an
+ *    entry point takes a `layout` argument;
+ *  - functions returning int32 return 0 on success and non-zero on failure;
+ *    when `err` is non-NULL it then receives a malloc'ed message that the
+ *    caller releases with macboost_free_string;
+ *  - getters return -1 for a NULL handle.
+ * Every predict runs on NVIDIA sm_100a GPUs; there is no CPU fallback: on a
+ * machine without such a GPU the predict entry points fail with a message.
+ * Handles may be used from several threads; predicts on one handle and one
+ * GPU are serialised.
+ */
+#ifndef MACBOOST_C_H
+#define MACBOOST_C_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference-compatible entry points --------------------------------- */
+
+/* Load a MacBoost JSON model file.  Replaces macboost_load,
+ * Sources/MacBoostC/CAPI.swift:257-271 (MacBooster.load, Booster.swift:2144-2162).
+ * Parses, validates and flattens the forest on the host; GPU replicas are
+ * created on first use (or by macboost_prepare).  Returns NULL on failure. */
+void *macboost_load(const char *path, char **err);
+
+/* Predict `rows` rows of feature-major x (rows*cols floats) into out
+ * (rows * num_classes floats, row-major).  Replaces macboost_predict,
+ * CAPI.swift:185-203: MacBooster.predict semantics (Booster.swift:1993-1999),
+ * i.e. raw margins, exp() for the poisson/tweedie objectives.  Fails for NULL
+ * arguments or cols != num_features.  Runs on the devices named by the
+ * MACBOOST_DEVICES environment variable ("0,1,..."), else the current one. */
+int32_t macboost_predict(void *handle, const float *x, int64_t rows, int64_t cols, float *out,
+                         char **err);
+
+/* Classes scored (outputs per row).  Replaces CAPI.swift:204-208. */
+int64_t macboost_num_classes(void *handle);
+/* Trees in the model.  Replaces CAPI.swift:272-277. */
+int64_t macboost_num_trees(void *handle);
+/* Features the model expects.  Replaces CAPI.swift:278-283. */
+int64_t macboost_num_features(void *handle);
+/* Best iteration; always 0 for a model read from a file.  Replaces CAPI.swift:284-289. */
+int64_t macboost_best_iteration(void *handle);
+/* Training warnings; always NULL for a model read from a file.  Replaces CAPI.swift:292-297. */
+char *macboost_warnings(void *handle);
+/* Feature importance (type 0 gain, 1 split count) into out[num_features].
+ * Replaces CAPI.swift:211-220 (MacBooster.featureImportance, Booster.swift:1926-1940). */
+int32_t macboost_feature_importance(void *handle, int32_t type, float *out);
+/* Write the model back as MacBoost JSON.  Replaces CAPI.swift:242-255. */
+int32_t macboost_save(void *handle, const char *path, char **err);
+/* Release a handle (NULL is ignored).  Replaces CAPI.swift:299-303. */
+void macboost_free(void *handle);
+/* Release a string returned through `err` or by macboost_warnings.
+ * Replaces CAPI.swift:305-308. */
+void macboost_free_string(char *s);
+
+/* Training-side entry points of the reference ABI (CAPI.swift:86-135,
+ * 138-183, 223-240).  This library is an inference engine: they exist so that
+ * bindings written for the full ABI load it unchanged, and they fail with a
+ * message ("not supported by this inference engine"). */
+void *macboost_train(const char *params_json, const float *x, int64_t rows, int64_t cols,
+                     int32_t row_major, const float *y, const float *w, const float *x_valid,
+                     int64_t valid_rows, const float *y_valid, char **err);
+int32_t macboost_select_features(const char *params_json, const float *x, int64_t rows,
+                                 int64_t cols, const float *y, const float *w, int32_t rounds,
+                                 int32_t trees, float alpha, int64_t seed, int32_t *out_hits,
+                                 int32_t *out_decision, float *out_gain_ratio, char **err);
+int32_t macboost_predict_contrib(void *handle, const float *x, int64_t rows, int64_t cols,
+                                 float *out, char **err);
+
+/* ---- additive entry points (no counterpart in the reference ABI) -------- */
+
+enum {
+  MACBOOST_KIND_PREDICT = 0, /* as macboost_predict */
+  MACBOOST_KIND_RAW = 1,     /* raw fp32 margins, rows x K */
+  MACBOOST_KIND_PROBA = 2,   /* predict_proba (__init__.py:433-445): rows x 2 [1-p, p] for
+                                one class, softmax rows x K otherwise; evaluated in float64,
+                                rounded to float32 */
+  MACBOOST_KIND_LEAF = 3     /* int32 heap index of the leaf reached, rows x num_trees */
+};
+enum { MACBOOST_LAYOUT_FEATURE_MAJOR = 0, MACBOOST_LAYOUT_ROW_MAJOR = 1 };
+
+/* Visible CUDA devices (0 if none or no driver). */
+int32_t macboost_device_count(void);
+
+/* Elements per output row for `kind` (-1 for a NULL handle / unknown kind). */
+int64_t macboost_output_cols(void *handle, int32_t kind);
+
+/* Predict from host memory.  Rows are split into contiguous shards over
+ * devices[0..ndev) (ndev == 0: current device), one model replica per GPU, no
+ * inter-GPU communication.  `out` holds rows * macboost_output_cols(kind)
+ * float32 (int32 for MACBOOST_KIND_LEAF).  Page-locked (pinned) x / out give
+ * overlapped transfers. */
+int32_t macboost_predict_ex(void *handle, const float *x, int64_t rows, int64_t cols,
+                            int32_t layout, int32_t kind, const int32_t *devices, int32_t ndev,
+                            void *out, char **err);
+
+/* Predict from device memory on `device`, enqueued on `stream` (a
+ * cudaStream_t; NULL = the legacy default stream) and returning before the
+ * work completes.  Feature-major x_dev is x_dev[f * ld + i] (ld >= rows);
+ * row-major x_dev is x_dev[i * cols + f] (ld ignored; this form waits for
+ * completion).  16-byte aligned x_dev with ld % 4 == 0 enables bulk staging.
+ * Kernel-side faults are reported by macboost_check_device. */
+int32_t macboost_predict_device(void *handle, int32_t device, const float *x_dev, int64_t rows,
+                                int64_t cols, int64_t ld, int32_t layout, int32_t kind,
+                                void *out_dev, void *stream, char **err);
+
+/* Upload the model to the listed devices now (otherwise done on first use). */
+int32_t macboost_prepare(void *handle, const int32_t *devices, int32_t ndev, char **err);
+
+/* Synchronise `device` and report kernel-side errors raised since the last check. */
+int32_t macboost_check_device(void *handle, int32_t device, char **err);
+
+/* Load a model from JSON text in memory (same rules as macboost_load). */
+void *macboost_load_json(const char *json, int64_t len, char **err);
+
+/* JSON description of the flattened forest and launch plan (free with
+ * macboost_free_string). */
+char *macboost_describe(void *handle);
+
+/* Forest-kernel launches issued by this process so far. */
+uint64_t macboost_kernel_launches(void);
+
+/* Page-locked host allocation for inputs and outputs (NULL on failure), and
+ * its release. */
+void *macboost_host_alloc(int64_t bytes);
+void macboost_host_free(void *p);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MACBOOST_C_H */

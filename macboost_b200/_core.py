@@ -1,0 +1,296 @@
+"""ctypes bridge to libmacboostc.so, the B200 inference engine's C ABI.
+
+Mirrors the predict subset of MacBoost's python/macboost/_core.py (library
+discovery through ``MACBOOST_LIB``, ``MacBoostError``, ``_take_error``,
+``_feature_major``, ``_Handle``, ``load`` / ``predict`` / getters) and adds
+the engine's additive entry points (output kinds, device lists, row-major and
+device-resident input, pinned host buffers).  No PyTorch, no CPU fallback: a
+missing library raises ``OSError``, and predicting without a B200 raises
+``MacBoostError`` from the library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import weakref
+from pathlib import Path
+
+import numpy as np
+
+KIND_PREDICT, KIND_RAW, KIND_PROBA, KIND_LEAF = 0, 1, 2, 3
+LAYOUT_FEATURE_MAJOR, LAYOUT_ROW_MAJOR = 0, 1
+
+_PKG = Path(__file__).resolve().parent
+
+
+def _find_library() -> str:
+    """MACBOOST_LIB, else the in-tree build (python -m macboost_b200.build)."""
+    candidates = []
+    if env := os.environ.get("MACBOOST_LIB"):
+        candidates.append(Path(env))
+    candidates.append(_PKG / "libmacboostc.so")
+    for c in candidates:
+        if c.is_file():
+            return str(c)
+    raise OSError("libmacboostc.so not found. Build it with `python -m macboost_b200.build` "
+                  "or set MACBOOST_LIB.")
+
+
+_c_char_pp = ctypes.POINTER(ctypes.c_char_p)
+_f32_p = ctypes.POINTER(ctypes.c_float)
+_i32_p = ctypes.POINTER(ctypes.c_int32)
+_lib_instance = None
+
+
+def _configure(lib):
+    P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    sig = {
+        "macboost_load": (P, [ctypes.c_char_p, _c_char_pp]),
+        "macboost_load_json": (P, [ctypes.c_char_p, I64, _c_char_pp]),
+        "macboost_predict": (I32, [P, _f32_p, I64, I64, _f32_p, _c_char_pp]),
+        "macboost_predict_ex": (I32, [P, P, I64, I64, I32, I32, _i32_p, I32, P, _c_char_pp]),
+        "macboost_predict_device": (I32, [P, I32, P, I64, I64, I64, I32, I32, P, P, _c_char_pp]),
+        "macboost_prepare": (I32, [P, _i32_p, I32, _c_char_pp]),
+        "macboost_check_device": (I32, [P, I32, _c_char_pp]),
+        "macboost_num_classes": (I64, [P]),
+        "macboost_num_trees": (I64, [P]),
+        "macboost_num_features": (I64, [P]),
+        "macboost_best_iteration": (I64, [P]),
+        "macboost_output_cols": (I64, [P, I32]),
+        "macboost_warnings": (P, [P]),
+        "macboost_feature_importance": (I32, [P, I32, _f32_p]),
+        "macboost_save": (I32, [P, ctypes.c_char_p, _c_char_pp]),
+        "macboost_free": (None, [P]),
+        "macboost_free_string": (None, [ctypes.c_char_p]),
+        "macboost_describe": (P, [P]),
+        "macboost_device_count": (I32, []),
+        "macboost_kernel_launches": (ctypes.c_uint64, []),
+        "macboost_host_alloc": (P, [I64]),
+        "macboost_host_free": (None, [P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+class _LazyLib:
+    def __getattr__(self, name):
+        global _lib_instance
+        if _lib_instance is None:
+            lib = ctypes.CDLL(_find_library())
+            _configure(lib)
+            _lib_instance = lib
+        return getattr(_lib_instance, name)
+
+
+_lib = _LazyLib()
+
+
+def native_available() -> bool:
+    try:
+        _lib.macboost_num_trees  # noqa: B018 -- probe the load
+        return True
+    except OSError:
+        return False
+
+
+def library_path() -> str:
+    return _find_library()
+
+
+class MacBoostError(RuntimeError):
+    pass
+
+
+def _take_error(err: ctypes.c_char_p) -> str:
+    msg = err.value.decode() if err.value else "unknown error"
+    _lib.macboost_free_string(err)
+    return msg
+
+
+def _feature_major(X) -> tuple[np.ndarray, int, int]:
+    """(n, f) array-like -> contiguous feature-major float32 + (rows, cols)."""
+    a = np.asarray(X, dtype=np.float32)
+    if a.ndim != 2:
+        raise ValueError(f"X must be 2-dimensional, got shape {a.shape}")
+    rows, cols = a.shape
+    return np.ascontiguousarray(a.T), rows, cols
+
+
+def _f32(a: np.ndarray):
+    return a.ctypes.data_as(_f32_p)
+
+
+class _Handle:
+    """Owns a model handle and frees it on GC."""
+
+    def __init__(self, ptr: int):
+        self.ptr = ptr
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            _lib.macboost_free(self.ptr)
+            self.ptr = None
+
+
+def load(path) -> _Handle:
+    err = ctypes.c_char_p()
+    ptr = _lib.macboost_load(str(path).encode(), ctypes.byref(err))
+    if not ptr:
+        raise MacBoostError(_take_error(err))
+    return _Handle(ptr)
+
+
+def load_json(text: str | bytes) -> _Handle:
+    data = text.encode() if isinstance(text, str) else bytes(text)
+    err = ctypes.c_char_p()
+    ptr = _lib.macboost_load_json(data, len(data), ctypes.byref(err))
+    if not ptr:
+        raise MacBoostError(_take_error(err))
+    return _Handle(ptr)
+
+
+def num_classes(handle: _Handle) -> int:
+    return _lib.macboost_num_classes(handle.ptr)
+
+
+def num_trees(handle: _Handle) -> int:
+    return _lib.macboost_num_trees(handle.ptr)
+
+
+def num_features(handle: _Handle) -> int:
+    return _lib.macboost_num_features(handle.ptr)
+
+
+def best_iteration(handle: _Handle) -> int:
+    return _lib.macboost_best_iteration(handle.ptr)
+
+
+def output_cols(handle: _Handle, kind: int) -> int:
+    return _lib.macboost_output_cols(handle.ptr, kind)
+
+
+def describe(handle: _Handle) -> str:
+    p = _lib.macboost_describe(handle.ptr)
+    s = ctypes.string_at(p).decode()
+    _lib.macboost_free_string(ctypes.cast(p, ctypes.c_char_p))
+    return s
+
+
+def device_count() -> int:
+    return _lib.macboost_device_count()
+
+
+def kernel_launches() -> int:
+    return _lib.macboost_kernel_launches()
+
+
+def predict(handle: _Handle, X) -> np.ndarray:
+    """The reference binding's predict (_core.py:210-220): feature-major copy
+    of X through macboost_predict; (rows,) for one class else (rows, K)."""
+    Xf, rows, cols = _feature_major(X)
+    k = _lib.macboost_num_classes(handle.ptr)
+    out = np.empty(rows * k, dtype=np.float32)
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict(handle.ptr, _f32(Xf), rows, cols, _f32(out), ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
+    return out.reshape(rows, k) if k > 1 else out
+
+
+def predict_ex(handle: _Handle, X, kind: int = KIND_PREDICT, layout: str = "row",
+               devices=None, out: np.ndarray | None = None) -> np.ndarray:
+    """Predict with an explicit output kind.
+
+    layout="row": X is (rows, F), passed without a host-side transpose (the
+    GPU transposes); layout="feature": X is (F, rows) feature-major.  Returns
+    (rows, output_cols(kind)) float32, or int32 for KIND_LEAF."""
+    a = np.asarray(X, dtype=np.float32)
+    if a.ndim != 2:
+        raise ValueError(f"X must be 2-dimensional, got shape {a.shape}")
+    a = np.ascontiguousarray(a)
+    if layout == "row":
+        rows, cols = a.shape
+        lay = LAYOUT_ROW_MAJOR
+    elif layout == "feature":
+        cols, rows = a.shape
+        lay = LAYOUT_FEATURE_MAJOR
+    else:
+        raise ValueError("layout must be 'row' or 'feature'")
+    ncol = _lib.macboost_output_cols(handle.ptr, kind)
+    if ncol < 0:
+        raise ValueError(f"unknown output kind {kind}")
+    dt = np.int32 if kind == KIND_LEAF else np.float32
+    if out is None:
+        out = np.empty((rows, ncol), dtype=dt)
+    elif out.dtype != dt or out.size < rows * ncol or not out.flags.c_contiguous:
+        raise ValueError("out has the wrong dtype, size or layout")
+    devs = None
+    nd = 0
+    if devices:
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        nd = len(devices)
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict_ex(handle.ptr, a.ctypes.data, rows, cols, lay, kind, devs, nd,
+                                  out.ctypes.data, ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
+    return out
+
+
+def predict_device(handle: _Handle, device: int, x_ptr: int, rows: int, cols: int, ld: int,
+                   out_ptr: int, kind: int = KIND_RAW, layout: int = LAYOUT_FEATURE_MAJOR,
+                   stream: int = 0) -> None:
+    """Enqueue a predict on device buffers (raw pointers) on `stream`."""
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict_device(handle.ptr, device, x_ptr, rows, cols, ld, layout, kind,
+                                      out_ptr, stream or None, ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
+
+
+def prepare(handle: _Handle, devices=None) -> None:
+    devs = None
+    nd = 0
+    if devices:
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        nd = len(devices)
+    err = ctypes.c_char_p()
+    if _lib.macboost_prepare(handle.ptr, devs, nd, ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+
+
+def check_device(handle: _Handle, device: int) -> None:
+    err = ctypes.c_char_p()
+    if _lib.macboost_check_device(handle.ptr, device, ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+
+
+def feature_importance(handle: _Handle, importance_type: str) -> np.ndarray:
+    n = _lib.macboost_num_features(handle.ptr)
+    out = np.empty(n, dtype=np.float32)
+    t = 1 if importance_type == "split" else 0
+    if _lib.macboost_feature_importance(handle.ptr, t, _f32(out)) != 0:
+        raise MacBoostError("feature_importance failed")
+    return out
+
+
+def save(handle: _Handle, path) -> None:
+    err = ctypes.c_char_p()
+    if _lib.macboost_save(handle.ptr, str(path).encode(), ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+
+
+def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
+    """A numpy array in page-locked host memory (freed with the array)."""
+    dtype = np.dtype(dtype)
+    nbytes = int(np.prod(shape)) * dtype.itemsize
+    ptr = _lib.macboost_host_alloc(max(nbytes, 1))
+    if not ptr:
+        raise MacBoostError(f"cannot allocate {nbytes} bytes of page-locked host memory")
+    buf = (ctypes.c_byte * max(nbytes, 1)).from_address(ptr)
+    arr = np.frombuffer(buf, dtype=dtype, count=int(np.prod(shape))).reshape(shape)
+    weakref.finalize(buf, _lib.macboost_host_free, ptr)
+    return arr

@@ -1,0 +1,269 @@
+// extern "C" boundary of libmacboostc.so (declared in include/macboost_c.h).
+//
+// Error behaviour follows Sources/MacBoostC/CAPI.swift: failures return -1
+// (NULL for constructors) and, when `err` is non-NULL, store a strdup'ed
+// message that the caller frees with macboost_free_string (CAPI.swift:77-80).
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/macboost_c.h"
+#include "engine.h"
+
+namespace {
+
+void set_error(char** err, const std::string& msg) {
+  if (err) *err = strdup(msg.c_str());
+}
+
+mb::Engine* engine(void* h) { return static_cast<mb::Engine*>(h); }
+
+// Devices for the reference-signature predict: MACBOOST_DEVICES="0,2,..."
+// when set, else the calling thread's current device.
+std::vector<int> default_devices() {
+  std::vector<int> d;
+  if (const char* s = std::getenv("MACBOOST_DEVICES")) {
+    const char* p = s;
+    while (*p) {
+      char* end = nullptr;
+      long v = std::strtol(p, &end, 10);
+      if (end == p) break;
+      d.push_back(int(v));
+      p = end;
+      while (*p == ',' || *p == ' ') ++p;
+    }
+  }
+  return d;
+}
+
+constexpr const char* kNoTraining = "not supported by this inference engine";
+
+}  // namespace
+
+extern "C" {
+
+void* macboost_load(const char* path, char** err) {
+  if (!path) {
+    set_error(err, "null path");
+    return nullptr;
+  }
+  std::string e;
+  mb::Engine* h = mb::engine_load(path, e);
+  if (!h) set_error(err, e);
+  return h;
+}
+
+void* macboost_load_json(const char* json, int64_t len, char** err) {
+  if (!json || len < 0) {
+    set_error(err, "null or empty JSON");
+    return nullptr;
+  }
+  std::string e;
+  mb::Engine* h = mb::engine_from_json(json, size_t(len), e);
+  if (!h) set_error(err, e);
+  return h;
+}
+
+int32_t macboost_predict(void* handle, const float* x, int64_t rows, int64_t cols, float* out,
+                         char** err) {
+  if (!handle || !x || !out) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::engine_predict_host(*engine(handle), x, rows, cols, 0, mb::kKindPredict,
+                              default_devices(), out, e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_predict_ex(void* handle, const float* x, int64_t rows, int64_t cols,
+                            int32_t layout, int32_t kind, const int32_t* devices, int32_t ndev,
+                            void* out, char** err) {
+  if (!handle || !x || !out || (ndev > 0 && !devices) || ndev < 0) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::vector<int> devs(devices, devices + ndev);
+  std::string e;
+  if (mb::engine_predict_host(*engine(handle), x, rows, cols, layout, kind, devs, out, e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_predict_device(void* handle, int32_t device, const float* x_dev, int64_t rows,
+                                int64_t cols, int64_t ld, int32_t layout, int32_t kind,
+                                void* out_dev, void* stream, char** err) {
+  if (!handle || !x_dev || !out_dev) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::engine_predict_device(*engine(handle), device, x_dev, rows, cols, ld, layout, kind,
+                                out_dev, static_cast<cudaStream_t>(stream), e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_prepare(void* handle, const int32_t* devices, int32_t ndev, char** err) {
+  if (!handle || (ndev > 0 && !devices) || ndev < 0) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::vector<int> devs(devices, devices + ndev);
+  if (devs.empty()) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    devs.push_back(cur);
+  }
+  for (int d : devs) {
+    std::string e;
+    if (!mb::engine_prepare(*engine(handle), d, e)) {
+      set_error(err, e);
+      return -1;
+    }
+  }
+  return 0;
+}
+
+int32_t macboost_check_device(void* handle, int32_t device, char** err) {
+  if (!handle) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::engine_check_device(*engine(handle), device, e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int64_t macboost_num_classes(void* handle) {
+  return handle ? int64_t(engine(handle)->model.K) : -1;
+}
+
+int64_t macboost_num_trees(void* handle) {
+  return handle ? int64_t(engine(handle)->model.trees.size()) : -1;
+}
+
+int64_t macboost_num_features(void* handle) {
+  return handle ? engine(handle)->model.num_features : -1;
+}
+
+int64_t macboost_best_iteration(void* handle) { return handle ? 0 : -1; }
+
+char* macboost_warnings(void* /*handle*/) { return nullptr; }
+
+int64_t macboost_output_cols(void* handle, int32_t kind) {
+  if (!handle || kind < mb::kKindPredict || kind > mb::kKindLeaf) return -1;
+  return mb::output_cols(*engine(handle), kind);
+}
+
+// MacBooster.featureImportance (Booster.swift:1926-1940): per feature, the
+// number of reachable splits or their summed gain, visiting each tree's nodes
+// in the reference's stack order so the float32 sums round identically.
+int32_t macboost_feature_importance(void* handle, int32_t type, float* out) {
+  if (!handle || !out) return -1;
+  const mb::Model& m = engine(handle)->model;
+  std::vector<float> imp(size_t(m.num_features), 0.0f);
+  for (const mb::Tree& t : m.trees) {
+    std::vector<int64_t> stack{0};
+    while (!stack.empty()) {
+      const int64_t n = stack.back();
+      stack.pop_back();
+      if (t.feature[size_t(n)] < 0) continue;
+      const size_t f = size_t(t.feature[size_t(n)]);
+      if (type == 1)
+        imp[f] += 1.0f;
+      else
+        imp[f] += size_t(n) < t.gain.size() ? t.gain[size_t(n)] : 0.0f;
+      stack.push_back(2 * n + 1);
+      stack.push_back(2 * n + 2);
+    }
+  }
+  std::memcpy(out, imp.data(), imp.size() * sizeof(float));
+  return 0;
+}
+
+int32_t macboost_save(void* handle, const char* path, char** err) {
+  if (!handle || !path) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  const std::string text = mb::model_to_json(engine(handle)->model);
+  FILE* f = std::fopen(path, "wb");
+  if (!f) {
+    set_error(err, std::string("cannot write '") + path + "'");
+    return -1;
+  }
+  const bool ok = std::fwrite(text.data(), 1, text.size(), f) == text.size();
+  const bool closed = std::fclose(f) == 0;
+  if (!ok || !closed) {
+    set_error(err, std::string("error writing '") + path + "'");
+    return -1;
+  }
+  return 0;
+}
+
+void macboost_free(void* handle) { delete engine(handle); }
+
+void macboost_free_string(char* s) { std::free(s); }
+
+char* macboost_describe(void* handle) {
+  if (!handle) return nullptr;
+  return strdup(engine(handle)->description.c_str());
+}
+
+int32_t macboost_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+uint64_t macboost_kernel_launches(void) { return mb::g_kernel_launches.load(); }
+
+void* macboost_host_alloc(int64_t bytes) {
+  void* p = nullptr;
+  if (bytes <= 0 || cudaHostAlloc(&p, size_t(bytes), cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return p;
+}
+
+void macboost_host_free(void* p) {
+  if (p) cudaFreeHost(p);
+}
+
+void* macboost_train(const char*, const float*, int64_t, int64_t, int32_t, const float*,
+                     const float*, const float*, int64_t, const float*, char** err) {
+  set_error(err, std::string("training is ") + kNoTraining);
+  return nullptr;
+}
+
+int32_t macboost_select_features(const char*, const float*, int64_t, int64_t, const float*,
+                                 const float*, int32_t, int32_t, float, int64_t, int32_t*,
+                                 int32_t*, float*, char** err) {
+  set_error(err, std::string("feature selection is ") + kNoTraining);
+  return 1;
+}
+
+int32_t macboost_predict_contrib(void*, const float*, int64_t, int64_t, float*, char** err) {
+  set_error(err, std::string("SHAP contributions are ") + kNoTraining);
+  return -1;
+}
+
+}  // extern "C"

@@ -1,0 +1,477 @@
+// Host engine (see engine.h).
+//
+// Predict from host memory, per GPU slice of rows:
+//   chunk c (double-buffered, two streams):  H2D copy of the chunk's used
+//   feature columns  ->  forest kernel  ->  D2H copy of the chunk's outputs.
+// The D2H of chunk c is enqueued after the copy and kernel of chunk c+1, so a
+// blocking copy into pageable host memory never stalls the next chunk.  Rows
+// shard into contiguous ranges over the GPUs, one host thread per GPU; the
+// model is replicated by host-to-device copy at prepare time and no
+// collective is needed (rows are independent).
+#include "engine.h"
+
+#include <algorithm>
+#include <cstring>
+#include <thread>
+
+namespace mb {
+
+std::atomic<unsigned long long> g_kernel_launches{0};
+
+namespace {
+
+std::string cuda_msg(const char* what, cudaError_t e) {
+  return std::string(what) + ": " + cudaGetErrorString(e);
+}
+
+#define MB_CUDA(call, what)                  \
+  do {                                       \
+    cudaError_t e_ = (call);                 \
+    if (e_ != cudaSuccess) {                 \
+      err = cuda_msg(what, e_);              \
+      return -1;                             \
+    }                                        \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int d) {
+    cudaGetDevice(&prev);
+    if (prev != d) cudaSetDevice(d);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <class T>
+int upload(T*& dst, const std::vector<T>& src, std::string& err) {
+  const size_t bytes = std::max<size_t>(src.size() * sizeof(T), 16);
+  MB_CUDA(cudaMalloc(reinterpret_cast<void**>(&dst), bytes), "cudaMalloc (model)");
+  if (!src.empty())
+    MB_CUDA(cudaMemcpy(dst, src.data(), src.size() * sizeof(T), cudaMemcpyHostToDevice),
+            "cudaMemcpy (model)");
+  return 0;
+}
+
+int ensure(void*& buf, size_t& cap, size_t bytes, std::string& err) {
+  if (bytes <= cap) return 0;
+  if (buf) cudaFree(buf);
+  buf = nullptr;
+  cap = 0;
+  MB_CUDA(cudaMalloc(&buf, bytes), "cudaMalloc (staging)");
+  cap = bytes;
+  return 0;
+}
+
+KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
+  const FlatForest& f = e.flat;
+  KArgs a{};
+  a.blob = d.blob;
+  a.block_off = d.block_off;
+  a.block_rec_base = d.block_rec_base;
+  a.masks = d.masks;
+  a.leaf_heap = d.leaf_heap;
+  a.base = d.base;
+  a.S = f.S;
+  a.K = f.K;
+  a.T = f.T;
+  a.G = f.G;
+  a.D = f.D;
+  a.Tb = f.plan.Tb;
+  a.nblocks = f.plan.nblocks;
+  a.buf_bytes = f.plan.buf_bytes;
+  a.leaf_off = f.leaf_off;
+  a.data_bins = e.model.num_bins - 1;
+  a.kind = kind;
+  a.log_link = e.model.uses_log_link() ? 1 : 0;
+  a.R = f.plan.R;
+  a.tile_bufs = f.plan.tile_bufs;
+  a.err = d.err;
+  return a;
+}
+
+// Launch the forest kernel over `rows` rows of feature-major `x` (stride ld).
+int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
+           const int* slot_feature, int kind, void* out, cudaStream_t s, std::string& err) {
+  if (rows <= 0) return 0;
+  KArgs a = make_args(e, d, kind);
+  a.x = x;
+  a.rows = rows;
+  a.ld = ld;
+  a.slot_feature = slot_feature;
+  a.bulk = (reinterpret_cast<uintptr_t>(x) % 16 == 0 && ld % 4 == 0) ? 1 : 0;
+  if (kind == kKindLeaf) {
+    a.out = nullptr;
+    a.out_leaf = static_cast<int*>(out);
+  } else {
+    a.out = static_cast<float*>(out);
+    a.out_leaf = nullptr;
+  }
+  a.ntiles = (rows + a.R - 1) / a.R;
+  const int grid = int(std::min<int64_t>(a.ntiles, d.grid_ctas));
+  cudaError_t ce = launch_forest(int(e.flat.layout), e.model.any_cat ? 1 : 0, a, e.flat.plan.smem,
+                                 grid, s);
+  if (ce != cudaSuccess) {
+    err = cuda_msg("forest kernel launch", ce);
+    return -1;
+  }
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return 0;
+}
+
+}  // namespace
+
+DeviceState::~DeviceState() {
+  if (device < 0) return;
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device);
+  for (auto* p : {static_cast<void*>(blob), static_cast<void*>(block_off),
+                  static_cast<void*>(block_rec_base), static_cast<void*>(slot_feature),
+                  static_cast<void*>(masks), static_cast<void*>(leaf_heap),
+                  static_cast<void*>(base), static_cast<void*>(err)})
+    if (p) cudaFree(p);
+  for (int i = 0; i < 2; ++i) {
+    if (xbuf[i]) cudaFree(xbuf[i]);
+    if (xraw[i]) cudaFree(xraw[i]);
+    if (obuf[i]) cudaFree(obuf[i]);
+    if (stream[i]) cudaStreamDestroy(stream[i]);
+  }
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+static Engine* finish_load(Engine* e, std::string& err) {
+  if (!flatten_forest(e->model, e->flat, err)) {
+    delete e;
+    return nullptr;
+  }
+  e->description = describe_forest(e->flat);
+  return e;
+}
+
+Engine* engine_load(const std::string& path, std::string& err) {
+  auto* e = new Engine();
+  if (!load_model_file(path, e->model, err)) {
+    delete e;
+    return nullptr;
+  }
+  return finish_load(e, err);
+}
+
+Engine* engine_from_json(const char* text, size_t len, std::string& err) {
+  auto* e = new Engine();
+  if (!parse_model_json(text, len, e->model, err)) {
+    delete e;
+    return nullptr;
+  }
+  return finish_load(e, err);
+}
+
+int64_t output_cols(const Engine& e, int kind) {
+  if (kind == kKindLeaf) return e.flat.T;
+  if (kind == kKindProba) return std::max(e.model.K, 2);
+  return e.model.K;
+}
+
+DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
+  std::lock_guard<std::mutex> lk(e.mu);
+  auto it = e.devices.find(device);
+  if (it != e.devices.end()) return it->second.get();
+  int ndev = 0;
+  cudaError_t ce = cudaGetDeviceCount(&ndev);
+  if (ce != cudaSuccess || ndev == 0) {
+    err = ce != cudaSuccess ? cuda_msg("no CUDA device available", ce)
+                            : std::string("no CUDA device available");
+    return nullptr;
+  }
+  if (device < 0 || device >= ndev) {
+    err = "device " + std::to_string(device) + " does not exist (" + std::to_string(ndev) +
+          " visible)";
+    return nullptr;
+  }
+  cudaDeviceProp prop{};
+  ce = cudaGetDeviceProperties(&prop, device);
+  if (ce != cudaSuccess) {
+    err = cuda_msg("cudaGetDeviceProperties", ce);
+    return nullptr;
+  }
+  if (prop.major != 10) {
+    err = "device " + std::to_string(device) + " is sm_" + std::to_string(prop.major) +
+          std::to_string(prop.minor) + "; this engine is built for sm_100a (B200)";
+    return nullptr;
+  }
+  if (size_t(prop.sharedMemPerBlockOptin) < e.flat.plan.smem) {
+    err = "device " + std::to_string(device) + " offers " +
+          std::to_string(prop.sharedMemPerBlockOptin) + " bytes of shared memory per block, " +
+          std::to_string(e.flat.plan.smem) + " needed";
+    return nullptr;
+  }
+  DeviceGuard g(device);
+  auto d = std::make_unique<DeviceState>();
+  d->device = device;
+  d->num_sms = prop.multiProcessorCount;
+  std::vector<float> base = e.model.base_scores;
+  std::vector<unsigned long long> boff(e.flat.block_off.begin(), e.flat.block_off.end());
+  if (boff.empty()) boff.push_back(0);
+  std::vector<unsigned> rec_base(e.flat.block_rec_base.begin(), e.flat.block_rec_base.end());
+  if (rec_base.empty()) rec_base.push_back(0);
+  std::vector<unsigned> masks(e.flat.full_masks.begin(), e.flat.full_masks.end());
+  std::vector<int> slots(e.flat.slot_feature.begin(), e.flat.slot_feature.end());
+  std::vector<int> heap(e.flat.leaf_heap.begin(), e.flat.leaf_heap.end());
+  if (upload(d->blob, e.flat.blob, err) || upload(d->block_off, boff, err) ||
+      upload(d->block_rec_base, rec_base, err) || upload(d->slot_feature, slots, err) ||
+      upload(d->masks, masks, err) || upload(d->leaf_heap, heap, err) ||
+      upload(d->base, base, err))
+    return nullptr;
+  if ((ce = cudaMalloc(reinterpret_cast<void**>(&d->err), sizeof(unsigned))) != cudaSuccess ||
+      (ce = cudaMemset(d->err, 0, sizeof(unsigned))) != cudaSuccess) {
+    err = cuda_msg("cudaMalloc (error word)", ce);
+    return nullptr;
+  }
+  for (int i = 0; i < 2; ++i)
+    if ((ce = cudaStreamCreateWithFlags(&d->stream[i], cudaStreamNonBlocking)) != cudaSuccess) {
+      err = cuda_msg("cudaStreamCreate", ce);
+      return nullptr;
+    }
+  int ctas = 0;
+  ce = forest_occupancy(int(e.flat.layout), e.model.any_cat ? 1 : 0, e.flat.K, e.flat.plan.R,
+                        e.flat.plan.smem, &ctas);
+  if (ce != cudaSuccess || ctas < 1) {
+    err = ce != cudaSuccess ? cuda_msg("occupancy query", ce)
+                            : std::string("the forest kernel cannot be resident on an SM");
+    return nullptr;
+  }
+  d->grid_ctas = ctas * d->num_sms;
+  if ((ce = cudaDeviceSynchronize()) != cudaSuccess) {
+    err = cuda_msg("model upload", ce);
+    return nullptr;
+  }
+  DeviceState* raw = d.get();
+  e.devices.emplace(device, std::move(d));
+  return raw;
+}
+
+namespace {
+
+int check_err_word(DeviceState& d, std::string& err) {
+  unsigned w = 0;
+  MB_CUDA(cudaMemcpy(&w, d.err, sizeof(w), cudaMemcpyDeviceToHost), "reading kernel status");
+  if (w != 0) {
+    cudaMemset(d.err, 0, sizeof(unsigned));
+    err = "device " + std::to_string(d.device) +
+          ": forest kernel gave up waiting for a shared-memory transfer (status " +
+          std::to_string(w) + ")";
+    return -1;
+  }
+  return 0;
+}
+
+// One GPU's share [r_begin, r_end) of a host-memory predict.
+int run_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t cols, int layout,
+              int kind, int64_t r_begin, int64_t r_end, void* out, std::string& err) {
+  std::lock_guard<std::mutex> lk(d.mu);
+  DeviceGuard g(d.device);
+  const int64_t n = r_end - r_begin;
+  if (n <= 0) return 0;
+  const FlatForest& f = e.flat;
+  const int64_t S = f.S;
+  const int64_t ocols = output_cols(e, kind);
+  const size_t oelem = 4;
+  const int R = f.plan.R;
+  // chunk rows: a multiple of the tile rows, <= 256 MB of staged input and of
+  // output per buffer
+  const int64_t in_row = std::max<int64_t>(layout == 1 ? cols : S, 1) * 4;
+  const int64_t out_row = std::max<int64_t>(ocols, 1) * int64_t(oelem);
+  const int64_t budget = int64_t(256) << 20;
+  int64_t C = std::min(budget / in_row, budget / out_row);
+  C = std::max<int64_t>(C / R * R, R);
+  if (C > n) C = (n + 3) / 4 * 4;
+  const int64_t ldc = (C + 3) / 4 * 4;
+  for (int p = 0; p < 2; ++p) {
+    if (ensure(reinterpret_cast<void*&>(d.xbuf[p]), d.xcap[p],
+               size_t(std::max<int64_t>(layout == 1 ? cols : S, 1)) * ldc * 4, err))
+      return -1;
+    if (layout == 1 &&
+        ensure(reinterpret_cast<void*&>(d.xraw[p]), d.rcap[p], size_t(cols) * C * 4 + 16, err))
+      return -1;
+    if (ensure(d.obuf[p], d.ocap[p], size_t(ocols) * C * oelem + 16, err)) return -1;
+  }
+  // runs of consecutive used features (one 2-D copy each)
+  std::vector<std::pair<int64_t, int64_t>> runs;  // (first feature, count)
+  for (int64_t s = 0; s < S; ++s) {
+    const int64_t feat = f.slot_feature[size_t(s)];
+    if (!runs.empty() && runs.back().first + runs.back().second == feat)
+      ++runs.back().second;
+    else
+      runs.push_back({feat, 1});
+  }
+  int64_t prev_r0 = -1, prev_n = 0;
+  int prev_p = 0;
+  auto drain = [&](int p, int64_t r0, int64_t nr) -> int {
+    char* dst = static_cast<char*>(out) + size_t(r0) * ocols * oelem;
+    MB_CUDA(cudaMemcpyAsync(dst, d.obuf[p], size_t(nr) * ocols * oelem, cudaMemcpyDeviceToHost,
+                            d.stream[p]),
+            "cudaMemcpyAsync (output)");
+    return 0;
+  };
+  int c = 0;
+  for (int64_t r0 = r_begin; r0 < r_end; r0 += C, ++c) {
+    const int p = c & 1;
+    const int64_t nr = std::min(C, r_end - r0);
+    cudaStream_t s = d.stream[p];
+    const int* slot_map = nullptr;
+    if (layout == 0) {
+      int64_t slot = 0;
+      for (auto& run : runs) {
+        MB_CUDA(cudaMemcpy2DAsync(d.xbuf[p] + slot * ldc, size_t(ldc) * 4,
+                                  x + run.first * rows + r0, size_t(rows) * 4, size_t(nr) * 4,
+                                  size_t(run.second), cudaMemcpyHostToDevice, s),
+                "cudaMemcpy2DAsync (features)");
+        slot += run.second;
+      }
+    } else {
+      MB_CUDA(cudaMemcpyAsync(d.xraw[p], x + r0 * cols, size_t(nr) * cols * 4,
+                              cudaMemcpyHostToDevice, s),
+              "cudaMemcpyAsync (rows)");
+      MB_CUDA(launch_transpose(d.xraw[p], nr, int(cols), d.xbuf[p], ldc, s), "transpose launch");
+      slot_map = d.slot_feature;
+    }
+    if (launch(e, d, d.xbuf[p], nr, ldc, slot_map, kind, d.obuf[p], s, err)) return -1;
+    if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
+    prev_r0 = r0;
+    prev_n = nr;
+    prev_p = p;
+  }
+  if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
+  MB_CUDA(cudaStreamSynchronize(d.stream[0]), "predict (stream 0)");
+  MB_CUDA(cudaStreamSynchronize(d.stream[1]), "predict (stream 1)");
+  return check_err_word(d, err);
+}
+
+}  // namespace
+
+int engine_predict_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
+                        int kind, const std::vector<int>& devices_in, void* out,
+                        std::string& err) {
+  if (rows < 0) {
+    err = "rows must be >= 0";
+    return -1;
+  }
+  if (cols != e.model.num_features) {
+    err = "model expects " + std::to_string(e.model.num_features) + " features, got " +
+          std::to_string(cols);
+    return -1;
+  }
+  if (layout != 0 && layout != 1) {
+    err = "layout must be 0 (feature-major) or 1 (row-major)";
+    return -1;
+  }
+  if (kind < kKindPredict || kind > kKindLeaf) {
+    err = "unknown output kind " + std::to_string(kind);
+    return -1;
+  }
+  if (rows == 0) return 0;
+  if (!x || !out) {
+    err = "null argument";
+    return -1;
+  }
+  std::vector<int> devices = devices_in;
+  if (devices.empty()) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    devices.push_back(cur);
+  }
+  std::vector<DeviceState*> ds;
+  for (int dev : devices) {
+    DeviceState* d = engine_prepare(e, dev, err);
+    if (!d) return -1;
+    if (std::find(ds.begin(), ds.end(), d) != ds.end()) {
+      err = "device " + std::to_string(dev) + " listed twice";
+      return -1;
+    }
+    ds.push_back(d);
+  }
+  const int nd = int(ds.size());
+  if (nd == 1) return run_slice(e, *ds[0], x, rows, cols, layout, kind, 0, rows, out, err);
+  std::vector<std::string> errs(static_cast<size_t>(nd));
+  std::vector<int> rcs(static_cast<size_t>(nd), 0);
+  std::vector<std::thread> th;
+  for (int g = 0; g < nd; ++g) {
+    const int64_t a = rows * g / nd, b = rows * (g + 1) / nd;
+    try {
+      th.emplace_back([&, g, a, b] {
+        rcs[size_t(g)] = run_slice(e, *ds[size_t(g)], x, rows, cols, layout, kind, a, b, out,
+                                   errs[size_t(g)]);
+      });
+    } catch (...) {
+      rcs[size_t(g)] = run_slice(e, *ds[size_t(g)], x, rows, cols, layout, kind, a, b, out,
+                                 errs[size_t(g)]);
+    }
+  }
+  for (auto& t : th) t.join();
+  for (int g = 0; g < nd; ++g)
+    if (rcs[size_t(g)] != 0) {
+      err = errs[size_t(g)];
+      return -1;
+    }
+  return 0;
+}
+
+int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, int64_t cols,
+                          int64_t ld, int layout, int kind, void* out, cudaStream_t stream,
+                          std::string& err) {
+  if (rows < 0) {
+    err = "rows must be >= 0";
+    return -1;
+  }
+  if (cols != e.model.num_features) {
+    err = "model expects " + std::to_string(e.model.num_features) + " features, got " +
+          std::to_string(cols);
+    return -1;
+  }
+  if (kind < kKindPredict || kind > kKindLeaf) {
+    err = "unknown output kind " + std::to_string(kind);
+    return -1;
+  }
+  if (layout == 0 && ld < rows) {
+    err = "feature-major input needs ld >= rows";
+    return -1;
+  }
+  if (layout != 0 && layout != 1) {
+    err = "layout must be 0 (feature-major) or 1 (row-major)";
+    return -1;
+  }
+  if (rows == 0) return 0;
+  if (!x || !out) {
+    err = "null argument";
+    return -1;
+  }
+  DeviceState* d = engine_prepare(e, device, err);
+  if (!d) return -1;
+  DeviceGuard g(device);
+  if (layout == 0) return launch(e, *d, x, rows, ld, d->slot_feature, kind, out, stream, err);
+  // Row-major device input: transpose into this device's staging buffer first;
+  // the staging buffer is private to this call, so the call waits for it.
+  std::lock_guard<std::mutex> lk(d->mu);
+  const int64_t ldt = (rows + 3) / 4 * 4;
+  if (ensure(reinterpret_cast<void*&>(d->xbuf[0]), d->xcap[0],
+             size_t(std::max<int64_t>(cols, 1)) * ldt * 4, err))
+    return -1;
+  MB_CUDA(launch_transpose(x, rows, int(cols), d->xbuf[0], ldt, stream), "transpose launch");
+  if (launch(e, *d, d->xbuf[0], rows, ldt, d->slot_feature, kind, out, stream, err)) return -1;
+  MB_CUDA(cudaStreamSynchronize(stream), "predict (row-major device input)");
+  return 0;
+}
+
+int engine_check_device(Engine& e, int device, std::string& err) {
+  DeviceState* d = engine_prepare(e, device, err);
+  if (!d) return -1;
+  DeviceGuard g(device);
+  MB_CUDA(cudaDeviceSynchronize(), "device synchronize");
+  return check_err_word(*d, err);
+}
+
+}  // namespace mb

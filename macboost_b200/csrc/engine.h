@@ -1,0 +1,78 @@
+// Host engine: per-model state, per-device replicas and the predict pipelines.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "forest.h"
+#include "kernels.h"
+#include "model.h"
+
+namespace mb {
+
+// One model replicated on one GPU, plus that GPU's staging buffers.
+struct DeviceState {
+  int device = -1;
+  int num_sms = 0;
+  int grid_ctas = 0;                    // persistent CTAs for this model
+  cudaStream_t stream[2] = {nullptr, nullptr};
+  // model replica
+  unsigned char* blob = nullptr;
+  unsigned long long* block_off = nullptr;
+  unsigned* block_rec_base = nullptr;
+  int* slot_feature = nullptr;
+  unsigned* masks = nullptr;
+  int* leaf_heap = nullptr;
+  float* base = nullptr;
+  unsigned* err = nullptr;              // kernel error word
+  // staging for host-memory inputs (double-buffered chunks)
+  float* xbuf[2] = {nullptr, nullptr};  // feature-major chunk
+  size_t xcap[2] = {0, 0};
+  float* xraw[2] = {nullptr, nullptr};  // row-major chunk before transposition
+  size_t rcap[2] = {0, 0};
+  void* obuf[2] = {nullptr, nullptr};
+  size_t ocap[2] = {0, 0};
+  std::mutex mu;                        // one predict at a time per (model, device)
+  ~DeviceState();
+};
+
+struct Engine {
+  Model model;
+  FlatForest flat;
+  std::string description;
+  std::mutex mu;                        // guards `devices`
+  std::map<int, std::unique_ptr<DeviceState>> devices;
+};
+
+// Global count of forest-kernel launches (for benchmarking claims).
+extern std::atomic<unsigned long long> g_kernel_launches;
+
+Engine* engine_load(const std::string& path, std::string& err);
+Engine* engine_from_json(const char* text, size_t len, std::string& err);
+
+// Output elements per row for `kind` (K, max(K,2) for proba, T for leaf).
+int64_t output_cols(const Engine& e, int kind);
+
+// Upload the model to `device` (idempotent).  Returns the device state.
+DeviceState* engine_prepare(Engine& e, int device, std::string& err);
+
+// Predict from host memory, rows sharded over `devices`.
+int engine_predict_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
+                        int kind, const std::vector<int>& devices, void* out, std::string& err);
+
+// Enqueue a predict on device memory (asynchronous on `stream`).
+int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, int64_t cols,
+                          int64_t ld, int layout, int kind, void* out, cudaStream_t stream,
+                          std::string& err);
+
+// Synchronise `device` and report any kernel-side error since the last check.
+int engine_check_device(Engine& e, int device, std::string& err);
+
+}  // namespace mb

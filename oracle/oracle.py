@@ -1,0 +1,186 @@
+"""Parity oracle for MacBoost batch inference (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
+``bench.py`` import this module; the product (``macboost_b200``) never does.
+
+* The model JSON is read with Python's ``json`` module into numpy arrays, the
+  way the reference's ``PyModel.__init__`` reads it
+  (python/macboost/_pyinfer.py:22-46): floats go through float64 and are then
+  rounded to float32.  This keeps the oracle independent of the product's C++
+  parser.
+* Margins and leaf indices come from ``mbref.c``, a C restatement of
+  ``predictCPU`` (Sources/MacBoost/Booster.swift:2035-2117) with PyModel's
+  choices where the two differ (see the header of mbref.c).
+* Transforms restate the reference formulas: ``predict`` applies fp32 ``exp``
+  for the log-link objectives (Booster.swift:1993-1999, _pyinfer.py:91-95);
+  ``predict_proba`` evaluates sigmoid / softmax in float64
+  (python/macboost/__init__.py:439-445).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libmbref.so"
+
+LOG_LINK_OBJECTIVES = (5, 6)   # poisson, tweedie (Booster.swift:15)
+
+
+def build(force: bool = False) -> Path:
+    """Compile mbref.c into oracle/libmbref.so with gcc (no fast-math)."""
+    src = HERE / "mbref.c"
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        import subprocess
+        tmp = LIB_PATH.with_suffix(f".so.tmp{os.getpid()}")
+        subprocess.run(["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-ffp-contract=off",
+                        "-fno-fast-math", "-pthread", "-o", str(tmp), str(src), "-lm"],
+                       check=True)
+        os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        lib = ctypes.CDLL(str(LIB_PATH))
+        P = ctypes.c_void_p
+        lib.mbref_predict.restype = ctypes.c_int32
+        lib.mbref_predict.argtypes = [P, ctypes.c_int32, P, P, P, P, P, P, ctypes.c_int32,
+                                      ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64,
+                                      ctypes.c_int64, ctypes.c_int32, P, P, ctypes.c_int32]
+        _lib = lib
+    return _lib
+
+
+@dataclass
+class OracleModel:
+    objective: int
+    num_bins: int
+    num_features: int
+    num_classes: int
+    base_scores: np.ndarray      # float32[K]
+    tree_off: np.ndarray         # int64[T+1]
+    feature: np.ndarray          # int32[N]
+    threshold: np.ndarray        # float32[N]
+    leaf: np.ndarray             # float32[N]
+    flags: np.ndarray            # uint8[N]
+    catmask: np.ndarray          # uint32[N*8]
+    has_mask: np.ndarray         # uint8[T]
+
+    @property
+    def num_trees(self) -> int:
+        return len(self.tree_off) - 1
+
+
+def load_model(path) -> OracleModel:
+    """Read a MacBoost model.json the way PyModel does (_pyinfer.py:22-46)."""
+    with open(path) as fh:
+        m = json.load(fh)
+    return model_from_dict(m)
+
+
+def model_from_dict(m: dict) -> OracleModel:
+    if m.get("version") != 1:
+        raise ValueError("unsupported model file version")
+    K = int(m.get("numClasses") or 1)
+    base = np.asarray(m.get("baseScores") or [m["baseScore"]], dtype=np.float32)
+    feats, thrs, leaves, flags, masks, has = [], [], [], [], [], []
+    off = [0]
+    for t in m["trees"]:
+        f = np.asarray(t["feature"], dtype=np.int64).astype(np.int32)
+        n = len(f)
+        feats.append(f)
+        thrs.append(np.asarray(t["threshold"], dtype=np.float32))
+        leaves.append(np.asarray(t["leaf"], dtype=np.float32))
+        flags.append(np.asarray(t["flags"], dtype=np.uint8))
+        cm = np.asarray(t.get("catMask") or [], dtype=np.uint64).astype(np.uint32)
+        if cm.size:
+            masks.append(cm)
+            has.append(1)
+        else:
+            masks.append(np.zeros(n * 8, dtype=np.uint32))
+            has.append(0)
+        off.append(off[-1] + n)
+
+    def cat(parts, dt):
+        return np.concatenate(parts).astype(dt) if parts else np.zeros(0, dt)
+
+    return OracleModel(
+        objective=int(m["objective"]), num_bins=int(m["numBins"]),
+        num_features=int(m["numFeatures"]), num_classes=K, base_scores=base,
+        tree_off=np.asarray(off, dtype=np.int64), feature=cat(feats, np.int32),
+        threshold=cat(thrs, np.float32), leaf=cat(leaves, np.float32),
+        flags=cat(flags, np.uint8), catmask=cat(masks, np.uint32),
+        has_mask=np.asarray(has, dtype=np.uint8))
+
+
+def _ptr(a):
+    return a.ctypes.data if a is not None and a.size else None
+
+
+def predict_raw(model: OracleModel, X, layout: str = "row", want_leaf: bool = False,
+                nthreads: int | None = None):
+    """Raw fp32 margins (rows, K) [and int32 leaf heap indices (rows, T)].
+
+    layout="row": X is (rows, F) row-major; layout="feature": X is (F, rows)
+    feature-major, the reference C ABI's layout (CAPI.swift:5-6)."""
+    lib = _load()
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    if layout == "row":
+        rows, cols = X.shape
+        lay, ld = 1, cols
+    else:
+        cols, rows = X.shape
+        lay, ld = 0, rows
+    if cols != model.num_features:
+        raise ValueError(f"model expects {model.num_features} features, got {cols}")
+    K, T = model.num_classes, model.num_trees
+    out = np.empty((rows, K), dtype=np.float32)
+    leaf = np.empty((rows, T), dtype=np.int32) if want_leaf else None
+    nt = nthreads or os.cpu_count() or 1
+    rc = lib.mbref_predict(
+        _ptr(model.tree_off), T, _ptr(model.feature), _ptr(model.threshold),
+        _ptr(model.leaf), _ptr(model.flags), _ptr(model.catmask), _ptr(model.has_mask),
+        model.num_bins - 1, K, _ptr(model.base_scores), _ptr(X), rows, cols, ld, lay,
+        out.ctypes.data if rows else None, _ptr(leaf), nt)
+    if rc != 0:
+        raise RuntimeError("mbref_predict rejected its arguments")
+    return (out, leaf) if want_leaf else out
+
+
+def predict(model: OracleModel, raw: np.ndarray) -> np.ndarray:
+    """`predict` semantics on raw margins: fp32 exp for poisson/tweedie."""
+    if model.objective in LOG_LINK_OBJECTIVES:
+        return np.exp(raw.astype(np.float32))
+    return raw
+
+
+def predict_proba(raw: np.ndarray) -> np.ndarray:
+    """MacBoostClassifier.predict_proba formula (__init__.py:439-445), float64."""
+    raw = np.asarray(raw).astype(np.float64)
+    if raw.ndim == 2 and raw.shape[1] > 1:
+        e = np.exp(raw - raw.max(axis=1, keepdims=True))
+        return e / e.sum(axis=1, keepdims=True)
+    p = 1.0 / (1.0 + np.exp(-raw.reshape(-1)))
+    return np.column_stack([1 - p, p])
+
+
+def ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in fp32 units-in-the-last-place between two float32 arrays."""
+    a = np.ascontiguousarray(a, dtype=np.float32).view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, dtype=np.float32).view(np.int32).astype(np.int64)
+    a = np.where(a < 0, -(a & 0x7FFFFFFF), a)
+    b = np.where(b < 0, -(b & 0x7FFFFFFF), b)
+    return np.abs(a - b)

@@ -1,0 +1,214 @@
+"""GPU parity: the CUDA path through the C ABI against the reference's golden
+vectors and the oracle.
+
+Bars: leaf indices and raw margins bit-exact;
+transformed outputs (sigmoid / softmax / exp) within 2 ulp fp32 of the
+reference formula evaluated in float64 (python/macboost/__init__.py:439-445)
+or fp32 exp (Booster.swift:1995-1997, _pyinfer.py:93-95).
+"""
+
+import ctypes
+import json
+
+import numpy as np
+import pytest
+
+from conftest import (O, assert_bitwise, assert_ulp, golden_arrays, golden_names,
+                      golden_oracle_model, golden_text)
+from macboost_b200 import synth
+
+pytestmark = pytest.mark.gpu
+ULP = 2  # tolerance for transformed outputs, fp32 units in the last place
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_all_kinds(gpu, tmp_path, name):
+    core = gpu
+    g = golden_arrays(name)
+    path = tmp_path / "m.json"
+    path.write_text(golden_text(name))
+    h = core.load(path)
+    X = g["X"]
+    K = g["raw"].shape[1]
+    raw = core.predict_ex(h, X, kind=core.KIND_RAW)
+    assert_bitwise(raw, g["raw"], f"{name} raw")
+    raw_f = core.predict_ex(h, np.ascontiguousarray(X.T), kind=core.KIND_RAW, layout="feature")
+    assert_bitwise(raw_f, g["raw"], f"{name} raw (feature-major)")
+    leaf = core.predict_ex(h, X, kind=core.KIND_LEAF)
+    assert np.array_equal(leaf, g["leaf"].astype(np.int32)), f"{name} leaf indices"
+    pred = core.predict_ex(h, X, kind=core.KIND_PREDICT)
+    assert_ulp(pred, g["pred"], ULP, f"{name} predict")
+    if not name.endswith("poisson"):
+        assert_bitwise(pred, g["pred"], f"{name} predict (no transform)")
+    proba = core.predict_ex(h, X, kind=core.KIND_PROBA)
+    assert_ulp(proba, g["proba"].astype(np.float32), ULP, f"{name} proba")
+    # the reference-signature entry point (feature-major copy, macboost_predict)
+    ref_sig = core.predict(h, X)
+    assert_bitwise(ref_sig.reshape(-1, K), g["pred"], f"{name} macboost_predict")
+
+
+CFG_ROWS = {"cfg1": 20_000, "cfg2": 50_000, "cfg3": 20_000, "cfg4": 4_000, "cfg5": 6_000}
+
+
+@pytest.fixture(scope="module")
+def cfg_models():
+    return {}
+
+
+@pytest.mark.parametrize("cfg", ["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+def test_config_models_vs_oracle(gpu, oracle_built, cfg, cfg_models):
+    """Full-size models of the five benchmark configs on seeded row samples."""
+    core = gpu
+    model = synth.make_model(cfg)
+    text = synth.model_to_json(model)
+    h = core.load_json(text)
+    om = O.model_from_dict(json.loads(text))
+    n = CFG_ROWS[cfg]
+    X = synth.make_data(cfg, rows=n, row_start=12_345, layout="feature")
+    raw_o, leaf_o = O.predict_raw(om, X, layout="feature", want_leaf=True)
+    raw = core.predict_ex(h, X, kind=core.KIND_RAW, layout="feature")
+    assert_bitwise(raw, raw_o, f"{cfg} raw")
+    leaf = core.predict_ex(h, X, kind=core.KIND_LEAF, layout="feature")
+    assert np.array_equal(leaf, leaf_o), f"{cfg} leaf"
+    proba = core.predict_ex(h, X, kind=core.KIND_PROBA, layout="feature")
+    ref = O.predict_proba(raw_o if om.num_classes > 1 else raw_o[:, 0]).astype(np.float32)
+    assert_ulp(proba, ref, ULP, f"{cfg} proba")
+
+
+@pytest.mark.parametrize("rows", [1, 3, 4, 31, 255, 257, 511, 513, 1000, 4099])
+def test_ragged_row_counts(gpu, oracle_built, rows):
+    core = gpu
+    name = "cfg2_small"
+    h = core.load_json(golden_text(name))
+    om = golden_oracle_model(name)
+    X = synth.make_data("cfg2", rows=rows, row_start=777, layout="row")
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), O.predict_raw(om, X),
+                   f"rows={rows}")
+
+
+def test_zero_rows(gpu):
+    core = gpu
+    h = core.load_json(golden_text("cfg1_small"))
+    out = core.predict_ex(h, np.zeros((0, 100), np.float32), kind=core.KIND_RAW)
+    assert out.shape == (0, 1)
+
+
+def test_device_entry_point_alignment_paths(gpu, oracle_built):
+    """Device-resident input: aligned (bulk copies) and misaligned (plain
+    loads) base addresses and strides give identical results."""
+    core = gpu
+    from macboost_b200 import _core
+    cudart = _cudart()
+    h = core.load_json(golden_text("cfg3_small"))
+    om = golden_oracle_model("cfg3_small")
+    rows, F = 3001, 100
+    X = synth.make_data("cfg3", rows=rows, layout="feature")
+    ref = O.predict_raw(om, X, layout="feature")
+    for ld, offset in [(3004, 0), (3001, 0), (3004, 1), (3010, 3)]:
+        buf = np.zeros((F, ld), np.float32)
+        buf[:, :rows] = X
+        flat = np.concatenate([np.zeros(offset, np.float32), buf.ravel()])
+        dx = cudart.alloc(flat.nbytes)
+        dout = cudart.alloc(rows * 4)
+        try:
+            cudart.h2d(dx, flat)
+            _core.predict_device(h, 0, dx + 4 * offset, rows, F, ld, dout, kind=core.KIND_RAW)
+            core.check_device(h, 0)
+            out = cudart.d2h(dout, rows, np.float32)
+        finally:
+            cudart.free(dx)
+            cudart.free(dout)
+        assert_bitwise(out.reshape(rows, 1), ref, f"ld={ld} offset={offset}")
+
+
+def test_deterministic_and_leaf_consistent(gpu):
+    core = gpu
+    h = core.load_json(golden_text("cfg4_small"))
+    X = synth.make_data("cfg4", rows=5000, layout="row")
+    a = core.predict_ex(h, X, kind=core.KIND_RAW)
+    b = core.predict_ex(h, X, kind=core.KIND_RAW)
+    assert_bitwise(a, b, "repeat")
+    # margins recomputed on the host from the GPU's leaf indices, in tree order
+    leaf = core.predict_ex(h, X, kind=core.KIND_LEAF)
+    m = json.loads(golden_text("cfg4_small"))
+    K = m["numClasses"]
+    acc = np.tile(np.asarray(m["baseScores"], np.float32), (X.shape[0], 1))
+    for t, tree in enumerate(m["trees"]):
+        lv = np.asarray(tree["leaf"], np.float64).astype(np.float32)
+        acc[:, t % K] += lv[leaf[:, t]]
+    assert_bitwise(a, acc, "margins from leaf indices")
+
+
+def test_multi_device_sharding(gpu, oracle_built):
+    core = gpu
+    n = core.device_count()
+    h = core.load_json(golden_text("cfg2_small"))
+    om = golden_oracle_model("cfg2_small")
+    X = synth.make_data("cfg2", rows=10_007, layout="row")
+    ref = O.predict_raw(om, X)
+    devs = list(range(min(n, 4)))
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW, devices=devs), ref,
+                   f"devices={devs}")
+    with pytest.raises(core.MacBoostError, match="listed twice"):
+        core.predict_ex(h, X, kind=core.KIND_RAW, devices=[0, 0])
+    with pytest.raises(core.MacBoostError, match="does not exist"):
+        core.predict_ex(h, X, kind=core.KIND_RAW, devices=[n + 3])
+
+
+def test_pinned_buffers(gpu, oracle_built):
+    core = gpu
+    h = core.load_json(golden_text("cfg1_small"))
+    om = golden_oracle_model("cfg1_small")
+    X = core.pinned_empty((7000, 100))
+    X[:] = synth.make_data("cfg1", rows=7000, layout="row")
+    out = core.pinned_empty((7000, 1))
+    core.predict_ex(h, X, kind=core.KIND_RAW, out=out)
+    assert_bitwise(out, O.predict_raw(om, np.asarray(X)), "pinned")
+
+
+class _Cudart:
+    """Minimal device-memory helpers over the CUDA runtime (test plumbing)."""
+
+    def __init__(self):
+        import glob
+        import os
+        cands = sorted(glob.glob("/usr/local/cuda/lib64/libcudart.so*")) + ["libcudart.so.12"]
+        last = None
+        for c in cands:
+            try:
+                self.lib = ctypes.CDLL(c if os.path.exists(c) else c)
+                break
+            except OSError as e:
+                last = e
+        else:
+            raise last
+        self.lib.cudaMalloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t]
+        self.lib.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.c_int]
+        self.lib.cudaFree.argtypes = [ctypes.c_void_p]
+
+    def alloc(self, n):
+        p = ctypes.c_void_p()
+        assert self.lib.cudaMalloc(ctypes.byref(p), n) == 0
+        return p.value
+
+    def h2d(self, d, a):
+        assert self.lib.cudaMemcpy(d, a.ctypes.data, a.nbytes, 1) == 0
+
+    def d2h(self, d, n, dt):
+        out = np.empty(n, dt)
+        assert self.lib.cudaMemcpy(out.ctypes.data, d, out.nbytes, 2) == 0
+        return out
+
+    def free(self, d):
+        self.lib.cudaFree(d)
+
+
+_CUDART = None
+
+
+def _cudart():
+    global _CUDART
+    if _CUDART is None:
+        _CUDART = _Cudart()
+    return _CUDART
