@@ -22,7 +22,7 @@ BUILD = PKG / "_build"
 LIB = PKG / "libmacboostc.so"
 
 CXX_SOURCES = ["model.cpp", "forest.cpp", "engine.cpp", "capi.cpp"]
-CU_SOURCES = ["kernels.cu"]
+CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -39,7 +39,7 @@ def _cuda_home(nvcc: str) -> Path:
 
 def _sources():
     return ([CSRC / s for s in CXX_SOURCES] + [CSRC / s for s in CU_SOURCES]
-            + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "macboost_c.h", Path(__file__)])
+            + sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "macboost_c.h", Path(__file__)])
 
 
 def needs_build() -> bool:

@@ -75,15 +75,19 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.masks = d.masks;
   a.leaf_heap = d.leaf_heap;
   a.base = d.base;
-  a.S = f.S;
+  a.S_stage = f.S_stage;
+  a.conv_src = d.conv_src;
+  a.conv_dst = d.conv_dst;
+  a.n_conv = int(f.conv_src.size());
   a.K = f.K;
-  a.T = f.T;
   a.G = f.G;
+  a.T = f.T;
   a.D = f.D;
   a.Tb = f.plan.Tb;
   a.nblocks = f.plan.nblocks;
   a.buf_bytes = f.plan.buf_bytes;
   a.leaf_off = f.leaf_off;
+  a.tile_bytes = f.plan.tile_bytes;
   a.data_bins = e.model.num_bins - 1;
   a.kind = kind;
   a.log_link = e.model.uses_log_link() ? 1 : 0;
@@ -95,13 +99,13 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
 
 // Launch the forest kernel over `rows` rows of feature-major `x` (stride ld).
 int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
-           const int* slot_feature, int kind, void* out, cudaStream_t s, std::string& err) {
+           const int* stage_feature, int kind, void* out, cudaStream_t s, std::string& err) {
   if (rows <= 0) return 0;
   KArgs a = make_args(e, d, kind);
   a.x = x;
   a.rows = rows;
   a.ld = ld;
-  a.slot_feature = slot_feature;
+  a.stage_feature = stage_feature;
   a.bulk = (reinterpret_cast<uintptr_t>(x) % 16 == 0 && ld % 4 == 0) ? 1 : 0;
   if (kind == kKindLeaf) {
     a.out = nullptr;
@@ -112,8 +116,8 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
   }
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = int(std::min<int64_t>(a.ntiles, d.grid_ctas));
-  cudaError_t ce = launch_forest(int(e.flat.layout), e.model.any_cat ? 1 : 0, a, e.flat.plan.smem,
-                                 grid, s);
+  cudaError_t ce = launch_forest(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, a,
+                                 e.flat.plan.smem, grid, s);
   if (ce != cudaSuccess) {
     err = cuda_msg("forest kernel launch", ce);
     return -1;
@@ -130,7 +134,8 @@ DeviceState::~DeviceState() {
   cudaGetDevice(&prev);
   cudaSetDevice(device);
   for (auto* p : {static_cast<void*>(blob), static_cast<void*>(block_off),
-                  static_cast<void*>(block_rec_base), static_cast<void*>(slot_feature),
+                  static_cast<void*>(block_rec_base), static_cast<void*>(stage_feature),
+                  static_cast<void*>(conv_src), static_cast<void*>(conv_dst),
                   static_cast<void*>(masks), static_cast<void*>(leaf_heap),
                   static_cast<void*>(base), static_cast<void*>(err)})
     if (p) cudaFree(p);
@@ -219,10 +224,13 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   std::vector<unsigned> rec_base(e.flat.block_rec_base.begin(), e.flat.block_rec_base.end());
   if (rec_base.empty()) rec_base.push_back(0);
   std::vector<unsigned> masks(e.flat.full_masks.begin(), e.flat.full_masks.end());
-  std::vector<int> slots(e.flat.slot_feature.begin(), e.flat.slot_feature.end());
+  std::vector<int> slots(e.flat.stage_feature.begin(), e.flat.stage_feature.end());
+  std::vector<int> csrc(e.flat.conv_src.begin(), e.flat.conv_src.end());
+  std::vector<int> cdst(e.flat.conv_dst.begin(), e.flat.conv_dst.end());
   std::vector<int> heap(e.flat.leaf_heap.begin(), e.flat.leaf_heap.end());
   if (upload(d->blob, e.flat.blob, err) || upload(d->block_off, boff, err) ||
-      upload(d->block_rec_base, rec_base, err) || upload(d->slot_feature, slots, err) ||
+      upload(d->block_rec_base, rec_base, err) || upload(d->stage_feature, slots, err) ||
+      upload(d->conv_src, csrc, err) || upload(d->conv_dst, cdst, err) ||
       upload(d->masks, masks, err) || upload(d->leaf_heap, heap, err) ||
       upload(d->base, base, err))
     return nullptr;
@@ -237,8 +245,8 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
       return nullptr;
     }
   int ctas = 0;
-  ce = forest_occupancy(int(e.flat.layout), e.model.any_cat ? 1 : 0, e.flat.K, e.flat.plan.R,
-                        e.flat.plan.smem, &ctas);
+  ce = forest_occupancy(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, e.flat.K,
+                        e.flat.G, e.flat.plan.R, e.flat.plan.smem, &ctas);
   if (ce != cudaSuccess || ctas < 1) {
     err = ce != cudaSuccess ? cuda_msg("occupancy query", ce)
                             : std::string("the forest kernel cannot be resident on an SM");
@@ -277,7 +285,7 @@ int run_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t c
   const int64_t n = r_end - r_begin;
   if (n <= 0) return 0;
   const FlatForest& f = e.flat;
-  const int64_t S = f.S;
+  const int64_t S = f.S_stage;
   const int64_t ocols = output_cols(e, kind);
   const size_t oelem = 4;
   const int R = f.plan.R;
@@ -302,7 +310,7 @@ int run_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t c
   // runs of consecutive used features (one 2-D copy each)
   std::vector<std::pair<int64_t, int64_t>> runs;  // (first feature, count)
   for (int64_t s = 0; s < S; ++s) {
-    const int64_t feat = f.slot_feature[size_t(s)];
+    const int64_t feat = f.stage_feature[size_t(s)];
     if (!runs.empty() && runs.back().first + runs.back().second == feat)
       ++runs.back().second;
     else
@@ -337,7 +345,7 @@ int run_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t c
                               cudaMemcpyHostToDevice, s),
               "cudaMemcpyAsync (rows)");
       MB_CUDA(launch_transpose(d.xraw[p], nr, int(cols), d.xbuf[p], ldc, s), "transpose launch");
-      slot_map = d.slot_feature;
+      slot_map = d.stage_feature;
     }
     if (launch(e, d, d.xbuf[p], nr, ldc, slot_map, kind, d.obuf[p], s, err)) return -1;
     if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
@@ -452,7 +460,7 @@ int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, i
   DeviceState* d = engine_prepare(e, device, err);
   if (!d) return -1;
   DeviceGuard g(device);
-  if (layout == 0) return launch(e, *d, x, rows, ld, d->slot_feature, kind, out, stream, err);
+  if (layout == 0) return launch(e, *d, x, rows, ld, d->stage_feature, kind, out, stream, err);
   // Row-major device input: transpose into this device's staging buffer first;
   // the staging buffer is private to this call, so the call waits for it.
   std::lock_guard<std::mutex> lk(d->mu);
@@ -461,7 +469,7 @@ int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, i
              size_t(std::max<int64_t>(cols, 1)) * ldt * 4, err))
     return -1;
   MB_CUDA(launch_transpose(x, rows, int(cols), d->xbuf[0], ldt, stream), "transpose launch");
-  if (launch(e, *d, d->xbuf[0], rows, ldt, d->slot_feature, kind, out, stream, err)) return -1;
+  if (launch(e, *d, d->xbuf[0], rows, ldt, d->stage_feature, kind, out, stream, err)) return -1;
   MB_CUDA(cudaStreamSynchronize(stream), "predict (row-major device input)");
   return 0;
 }

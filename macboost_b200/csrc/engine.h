@@ -27,7 +27,9 @@ struct DeviceState {
   unsigned char* blob = nullptr;
   unsigned long long* block_off = nullptr;
   unsigned* block_rec_base = nullptr;
-  int* slot_feature = nullptr;
+  int* stage_feature = nullptr;        // staged slot -> feature
+  int* conv_src = nullptr;             // -Inf plane fills
+  int* conv_dst = nullptr;
   unsigned* masks = nullptr;
   int* leaf_heap = nullptr;
   float* base = nullptr;

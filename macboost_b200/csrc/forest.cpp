@@ -2,23 +2,135 @@
 #include "forest.h"
 
 #include <algorithm>
+#include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
-#include <set>
 
 namespace mb {
+
+std::vector<int> group_options(int K) {
+  // (class count, tree group) pairs with a dedicated kernel instantiation
+  // (kernels_complete.cu / kernels_explicit.cu); other class counts use the
+  // generic kernel (per-thread accumulators in local memory, group 8).
+  switch (K) {
+    case 1: return {16, 8};
+    case 2: case 4: case 8: return {8};
+    case 3: case 6: return {6};
+    case 5: return {5};
+    case 7: return {7};
+    case 10: return {10};
+    case 12: return {12};
+    case 16: return {16};
+    default: return {8};
+  }
+}
+
+int max_threads_for_group(int G) { return G >= 12 ? 256 : 512; }
+
 namespace {
 
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Categorical node encoding shared by both layouts.  Codes run over
-// 0..dataBins (dataBins = the missing bin, _pyinfer.py:80-86); when every mask
-// bit from 32 to dataBins has the same value the mask compresses to word 0
-// plus that value.
-uint2_like encode_split(const Tree& t, int64_t o, uint32_t slot_field, int data_bins,
-                        std::vector<uint32_t>& full_masks) {
+// Optional restriction of the planner's choices from the environment, for
+// tuning: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0" (any subset; 0 = free).
+struct PlanOverride {
+  int G = 0, R = 0, bufs = 0, planes = -1;
+  PlanOverride() {
+    const char* s = std::getenv("MACBOOST_PLAN");
+    if (!s) return;
+    const char* p = s;
+    while (*p) {
+      const char* eq = std::strchr(p, '=');
+      if (!eq) break;
+      const std::string key(p, size_t(eq - p));
+      char* end = nullptr;
+      const long v = std::strtol(eq + 1, &end, 10);
+      if (key == "G") G = int(v);
+      else if (key == "R") R = int(v);
+      else if (key == "bufs") bufs = int(v);
+      else if (key == "planes") planes = int(v);
+      p = end;
+      while (*p == ',' || *p == ' ') ++p;
+    }
+  }
+};
+
+struct SlotPlan {
+  std::vector<int32_t> stage_feature;   // staged slot -> feature
+  std::vector<int32_t> raw_slot;        // feature -> staged slot (or -1)
+  std::vector<int32_t> left_slot;       // feature -> -Inf slot (planes) (or -1)
+  std::vector<int32_t> conv_src, conv_dst;
+  int S_stage = 0, S_total = 0;
+};
+
+// Which features are read, and by which kinds of split.
+void scan_usage(const Model& m, std::vector<char>& used, std::vector<char>& need_raw,
+                std::vector<char>& need_left) {
+  const size_t F = size_t(m.num_features);
+  used.assign(F, 0);
+  need_raw.assign(F, 0);
+  need_left.assign(F, 0);
+  for (const Tree& t : m.trees) {
+    std::vector<int64_t> st{0};
+    while (!st.empty()) {
+      const int64_t o = st.back();
+      st.pop_back();
+      const int32_t f = t.feature[size_t(o)];
+      if (f < 0) continue;
+      used[size_t(f)] = 1;
+      const uint32_t fl = t.flags[size_t(o)];
+      if ((fl & kFlagCategorical) && !t.cat_mask.empty())
+        need_raw[size_t(f)] = 1;  // categorical code from the raw value
+      else if (fl & kFlagDefaultLeft)
+        need_left[size_t(f)] = 1;
+      else
+        need_raw[size_t(f)] = 1;
+      st.push_back(2 * o + 1);
+      st.push_back(2 * o + 2);
+    }
+  }
+}
+
+SlotPlan make_slots(const Model& m, bool planes) {
+  std::vector<char> used, need_raw, need_left;
+  scan_usage(m, used, need_raw, need_left);
+  SlotPlan p;
+  const size_t F = size_t(m.num_features);
+  p.raw_slot.assign(F, -1);
+  p.left_slot.assign(F, -1);
+  for (size_t f = 0; f < F; ++f)
+    if (used[f]) {
+      p.raw_slot[f] = int32_t(p.stage_feature.size());
+      p.stage_feature.push_back(int32_t(f));
+    }
+  p.S_stage = int(p.stage_feature.size());
+  p.S_total = p.S_stage;
+  if (planes) {
+    for (size_t f = 0; f < F; ++f) {
+      if (!used[f] || !need_left[f]) continue;
+      if (need_raw[f]) {
+        p.left_slot[f] = p.S_total++;
+      } else {
+        p.left_slot[f] = p.raw_slot[f];  // only default-left splits: convert in place
+      }
+      p.conv_src.push_back(p.raw_slot[f]);
+      p.conv_dst.push_back(p.left_slot[f]);
+    }
+  }
+  return p;
+}
+
+// Categorical and numeric node encoding.  Codes run over 0..dataBins
+// (dataBins = the missing bin, _pyinfer.py:80-86); a mask whose bits 32 to
+// dataBins all share one value compresses to word 0 plus that value.
+uint2_like encode_split(const Tree& t, int64_t o, const SlotPlan& sp, bool planes, int R,
+                        int data_bins, std::vector<uint32_t>& full_masks) {
+  const int32_t f = t.feature[size_t(o)];
   const uint32_t fl = t.flags[size_t(o)];
+  const uint32_t row_bytes = uint32_t(R) * 4u;
   if ((fl & kFlagCategorical) && !t.cat_mask.empty()) {
+    const uint32_t off = uint32_t(sp.raw_slot[size_t(f)]) * row_bytes;
     const uint32_t* w = &t.cat_mask[size_t(o) * 8];
     bool uniform = true;
     uint32_t hb = 0;
@@ -27,42 +139,35 @@ uint2_like encode_split(const Tree& t, int64_t o, uint32_t slot_field, int data_
       for (int c = 33; c <= data_bins && uniform; ++c)
         uniform = ((w[c >> 5] >> (c & 31)) & 1u) == hb;
     }
-    if (uniform) return uint2_like{slot_field | kRecCategorical | (hb ? kRecDefaultLeft : 0u), w[0]};
+    if (uniform) return uint2_like{off | kRecCategorical | (hb ? kRecDefaultLeft : 0u), w[0]};
     const uint32_t idx = uint32_t(full_masks.size() / 8);
     full_masks.insert(full_masks.end(), w, w + 8);
-    return uint2_like{slot_field | kRecCategorical | kRecFullMask, idx};
+    return uint2_like{off | kRecCategorical | kRecFullMask, idx};
   }
   // Numeric (also a categorical flag in a tree without catMask: PyModel routes
   // it numerically, _pyinfer.py:79).
   uint32_t bits;
   std::memcpy(&bits, &t.threshold[size_t(o)], 4);
-  return uint2_like{slot_field | ((fl & kFlagDefaultLeft) ? kRecDefaultLeft : 0u), bits};
+  const bool dl = (fl & kFlagDefaultLeft) != 0;
+  if (planes) {
+    const int32_t s = dl ? sp.left_slot[size_t(f)] : sp.raw_slot[size_t(f)];
+    return uint2_like{uint32_t(s) * row_bytes, bits};
+  }
+  return uint2_like{uint32_t(sp.raw_slot[size_t(f)]) * row_bytes | (dl ? kRecDefaultLeft : 0u),
+                    bits};
 }
 
-struct Candidate {
-  int R, bufs;
-  bool resident;
-};
-// Preference: the whole forest resident in shared memory with double-buffered
-// row tiles; then resident with a single tile buffer; then the forest streamed
-// through two block buffers.
-const Candidate kCandidates[] = {{512, 2, true},  {256, 2, true},  {256, 1, true},
-                                 {128, 2, true},  {128, 1, true},  {256, 2, false},
-                                 {256, 1, false}, {128, 2, false}, {128, 1, false},
-                                 {64, 1, false},  {32, 1, false}};
-
-// Group the forest's trees into blocks.  `group_bytes(g0, ntrees)` is the
-// byte size of a block holding trees [g0, g0+ntrees) (ntrees a multiple of G;
-// trees past T are padding).  Returns false if a single group does not fit.
-bool make_blocks(int Tpad_groups, int G, size_t max_block,
-                 const std::function<size_t(int, int)>& block_bytes,
+// Group trees into blocks: `bytes(t0, n)` is the size of a block holding trees
+// [t0, t0+n) (n a multiple of G).  Returns false if one group does not fit.
+bool make_blocks(int ngroups, int G, size_t max_block,
+                 const std::function<size_t(int, int)>& bytes,
                  std::vector<std::pair<int, int>>& blocks) {
   blocks.clear();
   int g = 0;
-  while (g < Tpad_groups) {
+  while (g < ngroups) {
+    if (bytes(g * G, G) > max_block) return false;
     int n = 1;
-    if (block_bytes(g * G, G) > max_block) return false;
-    while (g + n < Tpad_groups && block_bytes(g * G, (n + 1) * G) <= max_block) ++n;
+    while (g + n < ngroups && bytes(g * G, (n + 1) * G) <= max_block) ++n;
     blocks.push_back({g * G, n * G});
     g += n;
   }
@@ -71,142 +176,196 @@ bool make_blocks(int Tpad_groups, int G, size_t max_block,
 
 }  // namespace
 
-bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
+bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_planes) {
   f = FlatForest();
   f.T = int(m.trees.size());
   f.K = m.K;
-  f.G = group_size(m.K);
   f.max_depth = m.max_depth;
   const int data_bins = m.num_bins - 1;
-
-  // Slots: the features some reachable split reads, in increasing order.
-  std::vector<int32_t> slot_of(size_t(m.num_features), -1);
-  {
-    std::vector<char> used(size_t(m.num_features), 0);
-    for (const Tree& t : m.trees) {
-      std::vector<int64_t> st{0};
-      while (!st.empty()) {
-        int64_t o = st.back();
-        st.pop_back();
-        if (t.feature[size_t(o)] < 0) continue;
-        used[size_t(t.feature[size_t(o)])] = 1;
-        st.push_back(2 * o + 1);
-        st.push_back(2 * o + 2);
-      }
-    }
-    for (int64_t i = 0; i < m.num_features; ++i)
-      if (used[size_t(i)]) {
-        slot_of[size_t(i)] = int32_t(f.slot_feature.size());
-        f.slot_feature.push_back(int32_t(i));
-      }
-  }
-  f.S = int(f.slot_feature.size());
-
   const bool complete = std::max(1, m.max_depth) <= kMaxCompleteDepth;
   f.layout = complete ? Layout::kComplete : Layout::kExplicit;
-  const int Tgroups = (f.T + f.G - 1) / f.G;
+  const int D = std::max(1, std::min(m.max_depth, 30));
+  const int NL = 1 << std::min(D, kMaxCompleteDepth);  // complete: slots / leaves per tree
 
-  // --- per-layout sizes --------------------------------------------------
-  const int D = std::max(1, m.max_depth);
-  const int NI = (1 << std::min(D, 30)) - 1, NL = 1 << std::min(D, 30);
-  std::vector<int64_t> tree_nodes;  // explicit: records per tree (padding trees: 1)
-  std::vector<size_t> node_prefix;  // explicit: prefix sums over padded trees
+  // explicit layout: reachable nodes per tree and the mean leaf depth
+  std::vector<int64_t> tree_nodes(size_t(f.T), 1);
+  double avg_depth = D;
   if (!complete) {
-    if (f.S > kMaxExplicitSlots) {
-      err = "explicit layout supports at most 4096 used features";
-      return false;
-    }
-    tree_nodes.assign(size_t(Tgroups) * f.G, 1);
+    double depth_sum = 0;
+    int64_t leaves = 0;
     for (int t = 0; t < f.T; ++t) {
-      int64_t cnt = 0;
-      std::vector<int64_t> st{0};
+      int64_t c = 0;
+      std::vector<std::pair<int64_t, int>> st{{0, 0}};
       while (!st.empty()) {
-        int64_t o = st.back();
+        auto [o, d] = st.back();
         st.pop_back();
-        ++cnt;
+        ++c;
         if (m.trees[size_t(t)].feature[size_t(o)] >= 0) {
-          st.push_back(2 * o + 1);
-          st.push_back(2 * o + 2);
+          st.push_back({2 * o + 1, d + 1});
+          st.push_back({2 * o + 2, d + 1});
+        } else {
+          depth_sum += d;
+          ++leaves;
         }
       }
-      if (cnt > kMaxExplicitNodes) {
-        err = "tree " + std::to_string(t) + " has more than 65535 reachable nodes";
+      if (c > kMaxExplicitNodes) {
+        err = "tree " + std::to_string(t) + " has more than 16384 reachable nodes";
         return false;
       }
-      tree_nodes[size_t(t)] = cnt;
+      tree_nodes[size_t(t)] = c;
     }
-    node_prefix.assign(tree_nodes.size() + 1, 0);
-    for (size_t i = 0; i < tree_nodes.size(); ++i)
-      node_prefix[i + 1] = node_prefix[i] + size_t(tree_nodes[i]);
+    avg_depth = leaves ? depth_sum / double(leaves) : 1.0;
   }
-  auto block_bytes = [&](int t0, int n) -> size_t {
-    if (complete) return round_up(round_up(size_t(n) * NI * 8, 16) + size_t(n) * NL * 4, 16);
-    const size_t head = round_up(16 + 4 * size_t(n), 16);
-    return round_up(head + 8 * (node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)]), 16);
-  };
 
-  // --- launch plan -------------------------------------------------------
-  std::vector<std::pair<int, int>> blocks;
-  LaunchPlan plan;
-  const int64_t S = std::max(f.S, 1);  // one slot even when no split reads a feature
-  for (const Candidate& c : kCandidates) {
-    const size_t tile = round_up(size_t(S) * c.R * 4, 128);
-    const size_t used = kSmemHeader + size_t(c.bufs) * tile;
-    if (used > kSmemBudget) continue;
-    const size_t avail = kSmemBudget - used;
-    if (Tgroups == 0) {
-      plan = LaunchPlan{c.R, c.bufs, 0, 0, 0, used, "no trees"};
-      blocks.clear();
-      break;
+  // --- launch plan: enumerate (group, rows per tile, buffers, planes) ------
+  const SlotPlan sp_planes = make_slots(m, true);
+  const SlotPlan sp_flat = make_slots(m, false);
+  const bool any_left = !sp_planes.conv_dst.empty();
+  struct Best {
+    LaunchPlan p;
+    int G = 0;
+    std::vector<std::pair<int, int>> blocks;
+    std::vector<size_t> node_prefix;
+    double cost = 1e300;
+  } best;
+  const int Rs[] = {512, 384, 256, 128, 64, 32};
+  const PlanOverride ov;
+  if (ov.planes >= 0 && force_planes < 0) force_planes = ov.planes;
+  for (int G : group_options(m.K)) {
+    if (ov.G && G != ov.G) continue;
+    const int ngroups = (f.T + G - 1) / G;
+    std::vector<size_t> node_prefix;  // explicit: prefix sums over padded trees
+    if (!complete) {
+      node_prefix.assign(size_t(ngroups) * G + 1, 0);
+      for (size_t i = 0; i + 1 < node_prefix.size(); ++i)
+        node_prefix[i + 1] = node_prefix[i] + size_t(i < tree_nodes.size() ? tree_nodes[i] : 1);
     }
-    if (c.resident) {
-      const size_t need = round_up(block_bytes(0, Tgroups * f.G), 128);
-      if (need > avail) continue;
-      blocks = {{0, Tgroups * f.G}};
-      plan = LaunchPlan{c.R, c.bufs, Tgroups * f.G, 1, uint32_t(need), used + need,
-                        "forest resident in shared memory"};
-      break;
+    auto block_bytes = [&](int t0, int n) -> size_t {
+      if (complete)
+        return round_up(round_up(size_t(n) * NL * 8, 128) + size_t(n) * NL * 4, 128);
+      const size_t head = round_up(16 + 4 * size_t(n), 16);
+      return round_up(head + 8 * (node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)]), 128);
+    };
+    for (int pl = 1; pl >= 0; --pl) {
+      const bool planes = pl == 1 && any_left;
+      if (pl == 0 && !any_left) continue;  // identical to the planes variant
+      if (force_planes == 0 && planes) continue;
+      if (force_planes == 1 && !planes && any_left) continue;
+      const SlotPlan& sp = planes ? sp_planes : sp_flat;
+      const int S_tile = std::max(sp.S_total, 1);
+      for (int R : Rs) {
+        if (R > max_threads_for_group(G) || (ov.R && R != ov.R)) continue;
+        for (int bufs = 2; bufs >= 1; --bufs) {
+          if (ov.bufs && bufs != ov.bufs) continue;
+          const size_t tile = round_up(size_t(S_tile) * R * 4, 128);
+          const size_t used = kSmemHeader + size_t(bufs) * tile;
+          if (used > kSmemBudget) continue;
+          const size_t avail = kSmemBudget - used;
+          LaunchPlan p;
+          p.R = R;
+          p.tile_bufs = bufs;
+          p.planes = planes;
+          p.tile_bytes = uint32_t(tile);
+          std::vector<std::pair<int, int>> blocks;
+          if (ngroups == 0) {
+            p.smem = used;
+            p.note = "no trees";
+          } else {
+            const size_t whole = round_up(block_bytes(0, ngroups * G), 128);
+            if (whole <= avail) {
+              blocks = {{0, ngroups * G}};
+              p.Tb = ngroups * G;
+              p.nblocks = 1;
+              p.buf_bytes = uint32_t(whole);
+              p.smem = used + whole;
+              p.note = "forest resident in shared memory";
+            } else {
+              const size_t max_block = (avail / 2) / 128 * 128;
+              if (complete) {
+                int Tb = 0;
+                for (int t = G; t <= ngroups * G && block_bytes(0, t) <= max_block; t += G) Tb = t;
+                if (Tb == 0) continue;
+                const int nb = (ngroups * G + Tb - 1) / Tb;
+                Tb = int(round_up(size_t((ngroups * G + nb - 1) / nb), size_t(G)));
+                for (int b = 0; b < nb; ++b) blocks.push_back({b * Tb, Tb});
+                p.Tb = Tb;
+              } else if (!make_blocks(ngroups, G, max_block, block_bytes, blocks)) {
+                continue;
+              }
+              size_t mx = 0;
+              for (auto& b : blocks) mx = std::max(mx, block_bytes(b.first, b.second));
+              p.nblocks = int(blocks.size());
+              p.buf_bytes = uint32_t(round_up(mx, 128));
+              p.smem = used + 2 * size_t(p.buf_bytes);
+              p.note = "forest streamed in tree blocks";
+            }
+          }
+          // Cost model (SM clocks per row), calibrated on B200 (cfg2-like
+          // depth-6 forests): a warp scores one tree in ~24 SM clocks when the
+          // shared-memory pipe is saturated (~19 wavefronts: two per 8-byte
+          // record load, one per gather, two for the leaf), ~36 without NaN
+          // planes (issue-bound on the default-left test); saturation needs
+          // warps more than per-thread tree groups: efficiency ~ (warps/16)^0.45
+          // * (G/8)^0.15.  Staging uses the SM's share of HBM bandwidth
+          // (~23 B/clk), hidden when double-buffered; streamed forest blocks
+          // add barriers and L2 traffic.
+          const int Tpad = blocks.empty() ? 0 : blocks.back().first + blocks.back().second;
+          const double levels = complete ? double(D) : avg_depth * 1.15;
+          const double per_tree = (planes || !any_left ? 24.0 : 36.0) * levels / 6.0 *
+                                  (complete ? 1.0 : 1.3);
+          const double warps = double(R) / 32.0;
+          const double eff =
+              std::min(1.0, std::pow(warps / 16.0, 0.45) * std::pow(double(G) / 8.0, 0.15));
+          const double compute = double(Tpad) * per_tree / 32.0 / eff;
+          const double load = double(sp.S_stage) * 4.0 / 23.0;
+          const double stream =
+              p.nblocks > 1
+                  ? (double(blocks.size()) * 1500.0 + double(p.buf_bytes) * p.nblocks / 64.0) /
+                        double(R)
+                  : 0.0;
+          const double cost = (bufs == 2 ? std::max(compute, load) : compute + load) + stream;
+          p.est_clk_per_row = cost;
+          if (cost < best.cost * 0.999) {
+            best.p = p;
+            best.G = G;
+            best.blocks = blocks;
+            best.node_prefix = node_prefix;
+            best.cost = cost;
+          }
+        }
+      }
     }
-    const size_t max_block = (avail / 2) / 128 * 128;
-    if (complete) {
-      // equal blocks: the largest multiple of G trees that fits, rebalanced
-      int Tb = 0;
-      for (int t = f.G; t <= Tgroups * f.G && block_bytes(0, t) <= max_block; t += f.G) Tb = t;
-      const int min_tb = (c.bufs > 1) ? std::min(4 * f.G, Tgroups * f.G) : f.G;
-      if (Tb < min_tb) continue;
-      const int nb = (Tgroups * f.G + Tb - 1) / Tb;
-      Tb = int(round_up(size_t((Tgroups * f.G + nb - 1) / nb), size_t(f.G)));
-      blocks.clear();
-      for (int b = 0; b < nb; ++b) blocks.push_back({b * Tb, Tb});
-      const size_t bb = round_up(block_bytes(0, Tb), 128);
-      plan = LaunchPlan{c.R, c.bufs, Tb, nb, uint32_t(bb), used + 2 * bb,
-                        "forest streamed in tree blocks"};
-      break;
-    }
-    if (!make_blocks(Tgroups, f.G, max_block, block_bytes, blocks)) continue;
-    const double avg = double(Tgroups * f.G) / double(blocks.size());
-    if (c.bufs > 1 && avg < 4.0 * f.G && blocks.size() > 1) continue;
-    size_t mx = 0;
-    for (auto& b : blocks) mx = std::max(mx, block_bytes(b.first, b.second));
-    mx = round_up(mx, 128);
-    plan = LaunchPlan{c.R, c.bufs, 0, int(blocks.size()), uint32_t(mx), used + 2 * mx,
-                      "forest streamed in tree blocks"};
-    break;
   }
-  if (plan.R == 0) {
-    err = "the forest's " + std::to_string(f.S) +
+  if (best.p.R == 0) {
+    err = "the forest's " + std::to_string(sp_flat.S_stage) +
           " used features do not fit a row tile in shared memory";
     return false;
   }
-  f.plan = plan;
+  f.plan = best.p;
+  f.G = best.G;
+  const std::vector<std::pair<int, int>>& blocks = best.blocks;
+  const std::vector<size_t>& node_prefix = best.node_prefix;
+  auto block_bytes = [&](int t0, int n) -> size_t {
+    if (complete)
+      return round_up(round_up(size_t(n) * NL * 8, 128) + size_t(n) * NL * 4, 128);
+    const size_t head = round_up(16 + 4 * size_t(n), 16);
+    return round_up(head + 8 * (node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)]), 128);
+  };
+  const SlotPlan& sp = f.plan.planes ? sp_planes : sp_flat;
+  f.S_stage = sp.S_stage;
+  f.S_total = sp.S_total;
+  f.stage_feature = sp.stage_feature;
+  f.conv_src = sp.conv_src;
+  f.conv_dst = sp.conv_dst;
+  const int R = f.plan.R;
   const int nb = int(blocks.size());
   f.Tpad = nb ? blocks.back().first + blocks.back().second : 0;
 
-  // --- emit ----------------------------------------------------------------
+  // --- emit ------------------------------------------------------------------
   f.block_off.assign(size_t(nb) + 1, 0);
   for (int b = 0; b < nb; ++b)
-    f.block_off[size_t(b) + 1] = f.block_off[size_t(b)] + block_bytes(blocks[size_t(b)].first,
-                                                                      blocks[size_t(b)].second);
+    f.block_off[size_t(b) + 1] =
+        f.block_off[size_t(b)] + block_bytes(blocks[size_t(b)].first, blocks[size_t(b)].second);
   f.blob.assign(size_t(f.block_off[size_t(nb)]), 0);
   const float neg_zero = -0.0f;
   uint32_t nz_bits;
@@ -214,22 +373,23 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
 
   if (complete) {
     f.D = D;
-    const int Tb = plan.Tb;
-    f.leaf_off = uint32_t(round_up(size_t(Tb) * NI * 8, 16));
+    const int Tb = f.plan.Tb;
+    f.leaf_off = uint32_t(round_up(size_t(Tb) * NL * 8, 128));
     f.leaf_heap.assign(size_t(f.Tpad) * NL, -1);
     for (int t = 0; t < f.Tpad; ++t) {
       const int b = t / Tb, i = t % Tb;
       uint8_t* blk = f.blob.data() + f.block_off[size_t(b)];
-      auto* recs = reinterpret_cast<uint2_like*>(blk) + size_t(i) * NI;
+      auto* slots = reinterpret_cast<uint2_like*>(blk) + size_t(i) * NL;  // heap n at n + 1
       auto* leaves = reinterpret_cast<float*>(blk + f.leaf_off) + size_t(i) * NL;
       int32_t* heap = f.leaf_heap.data() + size_t(t) * NL;
       if (t >= f.T) {
-        for (int n = 0; n < NI; ++n) recs[n] = uint2_like{0u, 0u};
+        for (int n = 0; n < NL; ++n) slots[n] = uint2_like{0u, 0u};
         for (int n = 0; n < NL; ++n) leaves[n] = neg_zero;
         continue;
       }
       const Tree& tr = m.trees[size_t(t)];
-      // (padded index p, original index o or -1, original leaf or -1, level)
+      const int NI = NL - 1;
+      // (padded heap index p, original index o or -1, original leaf or -1, level)
       std::function<void(int64_t, int64_t, int64_t, int)> fill = [&](int64_t p, int64_t o,
                                                                      int64_t lf, int L) {
         if (L == D) {
@@ -239,18 +399,19 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
           return;
         }
         if (lf < 0 && tr.feature[size_t(o)] >= 0) {
-          const uint32_t slot = uint32_t(slot_of[size_t(tr.feature[size_t(o)])]);
-          recs[p] = encode_split(tr, o, slot << 4, data_bins, f.full_masks);
+          slots[p + 1] = encode_split(tr, o, sp, f.plan.planes, R, data_bins, f.full_masks);
           fill(2 * p + 1, 2 * o + 1, -1, L + 1);
           fill(2 * p + 2, 2 * o + 2, -1, L + 1);
         } else {
+          // padding split: both subtrees end in the same leaf
           const int64_t leaf_src = lf >= 0 ? lf : o;
-          recs[p] = uint2_like{0u, 0u};
+          slots[p + 1] = uint2_like{0u, 0u};
           fill(2 * p + 1, -1, leaf_src, L + 1);
           fill(2 * p + 2, -1, leaf_src, L + 1);
         }
       };
       fill(0, 0, -1, 0);
+      f.nodes += int64_t(NL) * 2 - 1;
     }
   } else {
     f.leaf_heap.assign(node_prefix.back(), -1);
@@ -258,7 +419,7 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
     for (int b = 0; b < nb; ++b) {
       const int t0 = blocks[size_t(b)].first, n = blocks[size_t(b)].second;
       uint8_t* blk = f.blob.data() + f.block_off[size_t(b)];
-      uint32_t* head = reinterpret_cast<uint32_t*>(blk);
+      auto* head = reinterpret_cast<uint32_t*>(blk);
       head[0] = uint32_t(n);
       head[1] = uint32_t(t0);
       const size_t rec_off = round_up(16 + 4 * size_t(n), 16);
@@ -276,7 +437,6 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
           continue;
         }
         const Tree& tr = m.trees[size_t(t)];
-        // breadth-first, children of a node stored adjacently
         std::vector<int64_t> order{0};
         uint32_t next = 1;
         for (size_t q = 0; q < order.size(); ++q) {
@@ -288,9 +448,13 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
             heap[q] = int32_t(o);
             continue;
           }
-          const uint32_t slot = uint32_t(slot_of[size_t(tr.feature[size_t(o)])]);
-          uint2_like rec = encode_split(tr, o, slot << 4, data_bins, f.full_masks);
-          rec.x |= next << 16;
+          uint2_like rec = encode_split(tr, o, sp, f.plan.planes, R, data_bins, f.full_masks);
+          const uint32_t delta = next - uint32_t(q);
+          if (delta > kMaxChildDelta) {
+            err = "tree " + std::to_string(t) + " is too wide for the explicit layout";
+            return false;
+          }
+          rec.x |= delta << kRecChildShift;
           r[q] = rec;
           order.push_back(2 * o + 1);
           order.push_back(2 * o + 2);
@@ -306,13 +470,17 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err) {
 }
 
 std::string describe_forest(const FlatForest& f) {
+  char est[64];
+  std::snprintf(est, sizeof(est), "%.2f", f.plan.est_clk_per_row);
   std::string s = "{";
   s += "\"layout\":\"" + std::string(f.layout == Layout::kComplete ? "complete" : "explicit") + "\"";
   s += ",\"trees\":" + std::to_string(f.T);
   s += ",\"padded_trees\":" + std::to_string(f.Tpad);
   s += ",\"group\":" + std::to_string(f.G);
   s += ",\"classes\":" + std::to_string(f.K);
-  s += ",\"slots\":" + std::to_string(f.S);
+  s += ",\"slots\":" + std::to_string(f.S_stage);
+  s += ",\"tile_slots\":" + std::to_string(f.S_total);
+  s += ",\"nan_planes\":" + std::string(f.plan.planes ? "true" : "false");
   s += ",\"depth\":" + std::to_string(f.layout == Layout::kComplete ? f.D : f.max_depth);
   s += ",\"rows_per_tile\":" + std::to_string(f.plan.R);
   s += ",\"tile_buffers\":" + std::to_string(f.plan.tile_bufs);
@@ -321,6 +489,7 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"smem_bytes\":" + std::to_string(f.plan.smem);
   s += ",\"forest_bytes\":" + std::to_string(f.blob.size());
   s += ",\"full_masks\":" + std::to_string(f.full_masks.size() / 8);
+  s += ",\"est_clk_per_row\":" + std::string(est);
   s += ",\"plan\":\"" + f.plan.note + "\"";
   s += "}";
   return s;

@@ -2,32 +2,48 @@
 //
 // A MacBoost forest (implicit heaps, Booster.swift:119-146) is flattened once
 // per model into a byte blob of *tree blocks*; each block is staged into
-// shared memory with one bulk copy.  Only the features that some reachable
-// split uses are staged per row tile; they are renumbered into `slots`.
+// shared memory with bulk copies.  Rows are scored one per thread from a row
+// tile in shared memory that holds one 4*R-byte row per *slot*.
+//
+// Slots.  Every feature some reachable split reads gets one staging slot,
+// filled from HBM with a bulk copy of R consecutive values of that feature.
+// With NaN planes (the default), a feature read by a numeric split whose
+// missing values go LEFT also gets a second slot holding the same values with
+// NaN replaced by -Inf (each thread rewrites its own row of it after the tile
+// lands).  A numeric node then reads the slot of its default direction and
+// routes with a single unordered compare, right = !(v <= t):
+//   raw slot : NaN fails v <= t and goes right        (default right)
+//   -Inf slot: -Inf <= t for every finite threshold    (default left)
+// -Inf itself behaves identically in both slots.  Thresholds are finite
+// because the model file cannot hold anything else (JSON numbers that fit a
+// float32).  Without planes the default direction is a record flag instead.
 //
 // COMPLETE layout (forests no deeper than kMaxCompleteDepth).  Every tree is
 // padded to the forest depth D: a leaf reached at depth d < D becomes a
-// complete subtree whose 2^(D-d) leaves all carry that leaf's value (its heap
-// index is kept in a side table for leaf-index output), so each tree is a
-// fixed D steps of child = 2n + 1 + go_right.  A block of Tb trees holds
-//   records [Tb][2^D - 1]  uint2    internal nodes
-//   leaves  [Tb][2^D]      float    leaf values (at byte offset leaf_off)
+// complete subtree whose 2^(D-d) leaves all carry that leaf's value and heap
+// index, so each tree is a fixed D steps of child = 2n + 1 + go_right.  A
+// block of Tb trees holds
+//   records [Tb][2^D]  uint2   slot 0 unused, heap node n in slot n + 1, so
+//                               that every heap level starts on a 128-byte
+//                               line (conflict-free record loads)
+//   leaves  [Tb][2^D]  float   at byte offset leaf_off (128-aligned)
 //
 // EXPLICIT layout (deeper, sparse trees such as leaf-wise models).  The
 // reachable nodes of each tree are stored breadth-first with both children of
 // a node adjacent, so child = first_child + go_right.  A block holds
-//   tree_start [Tb]        uint32   first record of each tree (16-B padded)
-//   records    [...]       uint2
+//   header [4 + Tb]  uint32  [0] trees, [1] first tree index, [4 + i] first
+//                            record of tree i (padded to 16 bytes)
+//   records [...]    uint2
 // and blocks are variable-sized (block_off[] gives their byte offsets).
 //
 // Node record (uint2):
-//   x bits 0..2  flags  bit0: numeric node -> NaN goes left;
+//   x bits 0..2  flags  bit0: no-planes numeric node -> NaN goes left;
 //                             categorical node -> codes >= 32 go left
 //                       bit1: categorical split
 //                       bit2: categorical split with a full 256-bit mask
-//   x bit 3      explicit layout: leaf record (y = leaf value bits)
-//   x bits 4..   slot of the split feature (complete: bits 4..31;
-//                explicit: bits 4..15, first child in bits 16..31)
+//   x bits 7..17 byte offset of the slot row in the tile (a multiple of 4*R)
+//   x bits 18..31 explicit layout: index distance to the first child
+//   x == 0xFFFFFFFF explicit layout: leaf (y = leaf value bits)
 //   y            float bits of the threshold (numeric),
 //                mask bits 0..31 (categorical, bits 32..dataBins uniform),
 //                or the index of the node's 8-word mask (full mask).
@@ -52,35 +68,38 @@ struct uint2_like {
 constexpr uint32_t kRecDefaultLeft = 1u;
 constexpr uint32_t kRecCategorical = 2u;
 constexpr uint32_t kRecFullMask = 4u;
-constexpr uint32_t kRecLeaf = 8u;
+constexpr uint32_t kRecSlotMask = 0x3FF80u;   // bits 7..17
+constexpr uint32_t kRecLeaf = 0xFFFFFFFFu;    // explicit-layout leaf marker
+constexpr int kRecChildShift = 18;
+constexpr uint32_t kMaxChildDelta = 16383u;
 
 // Shared-memory budget per CTA on B200 (sm_100: 227 KB opt-in).
 constexpr size_t kSmemBudget = 232448;
-constexpr size_t kSmemHeader = 128;  // mbarriers + flags
+constexpr size_t kSmemHeader = 128;  // mbarriers
 
 // Deepest forest flattened to the complete layout.
 constexpr int kMaxCompleteDepth = 8;
-// Explicit layout limits: 12-bit slot, 16-bit child index.
-constexpr int64_t kMaxExplicitSlots = 4096;
-constexpr int64_t kMaxExplicitNodes = 65535;
+constexpr int64_t kMaxExplicitNodes = 16384;
 
 enum class Layout : int { kComplete = 0, kExplicit = 1 };
 
 // Trees walked concurrently by one thread (independent dependency chains).
-// A multiple of K so that tree j of a group always scores class j % K.
-inline int group_size(int K) {
-  if (K <= 0 || K > 16) return 8;
-  if (K >= 8) return K;
-  return K * (8 / K);
-}
+// Always a multiple of K, so that tree j of a group scores class j % K.  The
+// planner picks one of group_options(K); groups of 12 or more trees need the
+// register budget of at most max_threads_for_group(G) threads per CTA.
+std::vector<int> group_options(int K);
+int max_threads_for_group(int G);
 
 struct LaunchPlan {
   int R = 0;              // rows per tile == threads per CTA
   int tile_bufs = 0;      // 1 or 2 (double-buffered row tiles)
-  int Tb = 0;             // trees per block
+  bool planes = true;     // NaN planes (see above) or default-left flags
+  int Tb = 0;             // trees per block (complete layout)
   int nblocks = 0;        // blocks in the forest
   uint32_t buf_bytes = 0; // bytes of one forest buffer in shared memory
+  uint32_t tile_bytes = 0;// bytes of one row-tile buffer
   size_t smem = 0;        // dynamic shared memory bytes per CTA
+  double est_clk_per_row = 0;  // planner's estimate (SM clocks per row)
   std::string note;
 };
 
@@ -90,24 +109,26 @@ struct FlatForest {
   int Tpad = 0;           // incl. padding
   int G = 8;              // tree group size
   int K = 1;
-  int S = 0;              // staged feature slots
-  std::vector<int32_t> slot_feature;   // [S] model feature of each slot
+  int S_stage = 0;        // staged slots (one per used feature)
+  int S_total = 0;        // staged + -Inf slots
+  std::vector<int32_t> stage_feature;  // [S_stage] model feature of each staged slot
+  std::vector<int32_t> conv_src;       // -Inf slot fills: source slot ...
+  std::vector<int32_t> conv_dst;       // ... and destination slot (may be equal)
   LaunchPlan plan;
   std::vector<uint8_t> blob;           // all blocks
   std::vector<uint64_t> block_off;     // [nblocks + 1] byte offsets in blob
   std::vector<uint32_t> full_masks;    // [n][8]
   std::vector<int32_t> leaf_heap;      // complete: [Tpad][2^D]; explicit: [records]
-  // complete layout
-  int D = 0;
-  uint32_t leaf_off = 0;
-  // explicit layout: leaf_heap is indexed by (block record base + record)
-  std::vector<uint32_t> block_rec_base; // [nblocks] first record index of each block
+  std::vector<uint32_t> block_rec_base;// explicit: first record index of each block
+  int D = 0;                           // complete layout depth
+  uint32_t leaf_off = 0;               // complete layout: leaves offset in a block
   int max_depth = 0;
-  int64_t nodes = 0;                     // records in the blob (excl. padding)
+  int64_t nodes = 0;
 };
 
 // Flatten a validated model into the device layout and choose a launch plan.
-bool flatten_forest(const Model& m, FlatForest& out, std::string& err);
+// `force_planes`: -1 choose, 0 never, 1 always (when it fits).
+bool flatten_forest(const Model& m, FlatForest& out, std::string& err, int force_planes = -1);
 
 // Human-readable JSON description of a flattened forest.
 std::string describe_forest(const FlatForest& f);

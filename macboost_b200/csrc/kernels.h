@@ -1,5 +1,5 @@
-// Kernel-side argument block and launch entry points (implemented in
-// kernels.cu, called by the host engine).
+// Kernel-side argument block and launch entry points (implemented in the
+// kernels_*.cu files, called by the host engine).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -24,8 +24,11 @@ struct KArgs {
   const float* x;
   long long rows;
   long long ld;
-  int bulk;                        // 1: x, ld allow 16-byte bulk copies of row segments
-  const int* slot_feature;         // [S] feature of each staged slot, or null = identity
+  int bulk;                        // 1: x and ld allow 16-byte bulk copies of row runs
+  const int* stage_feature;        // [S_stage] feature of each staged slot, or null = identity
+  const int* conv_src;             // [n_conv] -Inf slot fills (src slot -> dst slot)
+  const int* conv_dst;
+  int S_stage, n_conv;
   // Forest (device copy of FlatForest).
   const unsigned char* blob;
   const unsigned long long* block_off;  // [nblocks + 1]
@@ -33,8 +36,8 @@ struct KArgs {
   const unsigned* masks;                // full categorical masks, 8 words each
   const int* leaf_heap;
   const float* base;                    // [K] starting margins
-  int S, K, T, G, D, Tb, nblocks;
-  unsigned buf_bytes, leaf_off;
+  int K, G, T, D, Tb, nblocks;      // G: trees walked at once per thread
+  unsigned buf_bytes, leaf_off, tile_bytes;
   int data_bins;
   // Output.
   int kind;
@@ -47,16 +50,17 @@ struct KArgs {
   unsigned* err;
 };
 
-// Launch the forest kernel for `layout` (0 complete, 1 explicit) on `stream`.
-// Returns the CUDA error of the launch.
-cudaError_t launch_forest(int layout, int cat, const KArgs& a, size_t smem, int grid,
-                          cudaStream_t stream);
+// Launch the forest kernel on `stream`.  layout: 0 complete, 1 explicit;
+// planes: NaN planes in the tile; cat: the model has categorical splits.
+cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,
+                          int grid, cudaStream_t stream);
+
+// Largest number of co-resident CTAs per SM for that kernel.
+cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
+                             size_t smem, int* ctas);
 
 // Row-major [rows][F] -> feature-major [F][ld] (ld >= rows).
 cudaError_t launch_transpose(const float* in, long long rows, int F, float* out, long long ld,
                              cudaStream_t stream);
-
-// Largest number of co-resident CTAs per SM for the given kernel and smem.
-cudaError_t forest_occupancy(int layout, int cat, int K, int R, size_t smem, int* ctas);
 
 }  // namespace mb

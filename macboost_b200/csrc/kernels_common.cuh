@@ -1,0 +1,336 @@
+// Device helpers shared by the forest kernels (see kernels_complete.cu for
+// the execution model).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "forest.h"
+#include "kernels.h"
+
+namespace mb {
+namespace dev {
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Threads per CTA the kernels are compiled for: groups of 12 or more trees
+// need the larger per-thread register budget (mb::max_threads_for_group).
+template <int G>
+struct Bounds {
+  static constexpr int kMaxThreads = G >= 12 ? 256 : 512;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Shared-memory accesses by 32-bit shared-window address.  `volatile` keeps
+// them in program order with respect to the mbarrier waits and barriers.
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 r;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+  return r;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts_f32(uint32_t a, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for phase `parity`; false (and *err |= timeout) after 2 s.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// Warp 0: stage the staged slots of row tile `tile` with bulk copies, one per
+// slot: R consecutive values of one feature (16-byte aligned, multiple of 16).
+__device__ __forceinline__ void issue_tile(const KArgs& a, long long tile, uint32_t dst,
+                                           uint32_t bar, int lane) {
+  const long long r0 = tile * a.R;
+  long long nv = a.rows - r0;
+  if (nv > a.R) nv = a.R;
+  const uint32_t nbytes = uint32_t(((nv + 3) & ~3ll) * 4);
+  if (lane == 0) mbar_arrive_expect_tx(bar, nbytes * uint32_t(a.S_stage));
+  __syncwarp();
+  for (int s = lane; s < a.S_stage; s += 32) {
+    const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
+    bulk_g2s(dst + uint32_t(s) * uint32_t(a.R) * 4u, a.x + f * a.ld + r0, nbytes, bar);
+  }
+}
+
+// All threads: stage a row tile with ordinary coalesced loads (when the input
+// address or stride does not allow bulk copies).
+__device__ __forceinline__ void load_tile_sync(const KArgs& a, long long tile, uint32_t dst) {
+  const long long row = tile * a.R + threadIdx.x;
+  const bool ok = row < a.rows;
+  for (int s = 0; s < a.S_stage; ++s) {
+    const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
+    sts_f32(dst + (uint32_t(s) * uint32_t(a.R) + threadIdx.x) * 4u,
+            ok ? __ldg(a.x + f * a.ld + row) : 0.0f);
+  }
+}
+
+// Each thread, its own row: fill the -Inf slots (NaN -> -Inf).
+__device__ __forceinline__ void fill_left_planes(const KArgs& a, uint32_t rowbase) {
+  for (int i = 0; i < a.n_conv; ++i) {
+    const uint32_t src = uint32_t(__ldg(a.conv_src + i)) * uint32_t(a.R) * 4u;
+    const uint32_t dst = uint32_t(__ldg(a.conv_dst + i)) * uint32_t(a.R) * 4u;
+    const float v = lds_f32(rowbase + src);
+    sts_f32(rowbase + dst, isnan(v) ? -__int_as_float(0x7f800000) : v);
+  }
+}
+
+// Warp 0: stage forest block b (16 KB bulk copies spread over the lanes).
+__device__ __forceinline__ void issue_block(const KArgs& a, int b, uint32_t dst, uint32_t bar,
+                                            int lane) {
+  const unsigned long long off = a.block_off[b];
+  const uint32_t bytes = uint32_t(a.block_off[b + 1] - off);
+  if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
+  __syncwarp();
+  constexpr uint32_t kChunk = 16384;
+  for (uint32_t o = uint32_t(lane) * kChunk; o < bytes; o += 32u * kChunk) {
+    const uint32_t n = (bytes - o < kChunk) ? (bytes - o) : kChunk;
+    bulk_g2s(dst + o, a.blob + off + o, n, bar);
+  }
+}
+
+// Routing decision: 1 = right child.  PLANES: numeric records address the
+// slot of their default direction and compare unordered; otherwise bit0 of
+// the record selects the ordered compare for default-left.  CAT: categorical
+// records (bit1) test the node's mask at the value's code.
+template <bool PLANES, bool CAT>
+__device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsigned* masks,
+                                          int data_bins) {
+  const uint32_t addr = rowbase + ((PLANES && !CAT) ? r.x : (r.x & kRecSlotMask));
+  const float v = lds_f32(addr);
+  if (CAT && (r.x & kRecCategorical)) {
+    int code = data_bins;                  // non-finite / out of range -> missing bin
+    if (isfinite(v)) {
+      const float q = rintf(v);            // round half to even
+      if (q >= 0.0f && q < float(data_bins)) code = int(q);
+    }
+    uint32_t left;
+    if (r.x & kRecFullMask)
+      left = (__ldg(masks + size_t(r.y) * 8 + (code >> 5)) >> (code & 31)) & 1u;
+    else
+      left = code < 32 ? (r.y >> code) & 1u : (r.x & kRecDefaultLeft);
+    return left ^ 1u;
+  }
+  const float t = __uint_as_float(r.y);
+  if (PLANES) return uint32_t(!(v <= t));
+  return (r.x & kRecDefaultLeft) ? uint32_t(v > t) : uint32_t(!(v <= t));
+}
+
+// Per-thread accumulators: KT compile-time classes, or (KT == 0) up to 128.
+template <int KT>
+struct Acc {
+  float v[KT];
+  __device__ __forceinline__ void init(const float* base, int) {
+#pragma unroll
+    for (int c = 0; c < KT; ++c) v[c] = __ldg(base + c);
+  }
+  __device__ __forceinline__ void add(int j, int, float l) { v[j % KT] += l; }
+  __device__ __forceinline__ float get(int c) const { return v[c]; }
+  __device__ __forceinline__ int k() const { return KT; }
+};
+template <>
+struct Acc<0> {
+  float v[128];
+  int K;
+  __device__ __forceinline__ void init(const float* base, int K_) {
+    K = K_;
+    for (int c = 0; c < K; ++c) v[c] = __ldg(base + c);
+  }
+  __device__ __forceinline__ void add(int, int t, float l) { v[t % K] += l; }
+  __device__ __forceinline__ float get(int c) const { return v[c]; }
+  __device__ __forceinline__ int k() const { return K; }
+};
+
+template <int KT>
+__device__ __forceinline__ void epilogue(const KArgs& a, const Acc<KT>& acc, long long row) {
+  if (a.out == nullptr) return;
+  const int K = acc.k();
+  float* o = a.out;
+  if (a.kind == kKindProba) {
+    if (K == 1) {
+      // MacBoostClassifier.predict_proba, binary (__init__.py:444-445), float64
+      const double p = 1.0 / (1.0 + exp(-double(acc.get(0))));
+      o[2 * row] = float(1.0 - p);
+      o[2 * row + 1] = float(p);
+    } else {
+      // softmax in float64 (__init__.py:440-442)
+      double m = double(acc.get(0));
+      for (int c = 1; c < K; ++c) m = fmax(m, double(acc.get(c)));
+      double s = 0.0;
+      for (int c = 0; c < K; ++c) s += exp(double(acc.get(c)) - m);
+      for (int c = 0; c < K; ++c) o[row * K + c] = float(exp(double(acc.get(c)) - m) / s);
+    }
+    return;
+  }
+  if (a.kind == kKindPredict && a.log_link) {
+    // poisson / tweedie mean, exp of the fp32 margin (Booster.swift:1995-1997)
+    for (int c = 0; c < K; ++c) o[row * K + c] = float(exp(double(acc.get(c))));
+    return;
+  }
+  for (int c = 0; c < K; ++c) o[row * K + c] = acc.get(c);
+}
+
+// The per-CTA pipeline shared by both layouts: a persistent loop over row
+// tiles (double- or single-buffered bulk staging), forest blocks (resident,
+// or streamed through two buffers), the -Inf plane fill, and the bounded-wait
+// abort protocol.  `score(fb, b, row, rowbase, acc)` walks every tree of the
+// forest block at shared address fb for this thread's row.
+template <int KT, class ScoreBlock>
+__device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, ScoreBlock score) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t bar_tile0 = base, bar_f0 = base + 16;
+  const uint32_t tiles = base + uint32_t(kSmemHeader);
+  const uint32_t fbuf = tiles + uint32_t(a.tile_bufs) * a.tile_bytes;
+  const bool streaming = a.nblocks > 1;
+  const bool bulk = a.bulk && a.S_stage > 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(base + 8u * i, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  long long tile = blockIdx.x;
+  if (tile >= a.ntiles) return;  // uniform over the CTA
+
+  if (warp == 0) {
+    if (a.nblocks > 0) issue_block(a, 0, fbuf, bar_f0, lane);
+    if (bulk) issue_tile(a, tile, tiles, bar_tile0, lane);
+  }
+  unsigned fseq = 0;  // forest blocks consumed by this CTA
+
+  for (int k = 0; tile < a.ntiles; tile += gridDim.x, ++k) {
+    const int tb = (a.tile_bufs == 2) ? (k & 1) : 0;
+    const uint32_t tl = tiles + uint32_t(tb) * a.tile_bytes;
+    const long long next = tile + gridDim.x;
+    if (bulk && a.tile_bufs == 2 && warp == 0 && next < a.ntiles) {
+      // buffer tb^1 held tile k-1, released by the barrier ending that iteration
+      if (lane == 0) fence_proxy_async();
+      __syncwarp();
+      issue_tile(a, next, tiles + uint32_t(tb ^ 1) * a.tile_bytes, bar_tile0 + 8u * (tb ^ 1),
+                 lane);
+    }
+    if (bulk) {
+      const uint32_t parity = (a.tile_bufs == 2) ? uint32_t((k >> 1) & 1) : uint32_t(k & 1);
+      const bool ok = mbar_wait(bar_tile0 + 8u * tb, parity, a.err);
+      if (__syncthreads_or(!ok)) return;
+    } else if (a.S_stage > 0) {
+      load_tile_sync(a, tile, tl);
+      __syncthreads();
+    }
+
+    const long long row = tile * a.R + tid;
+    const uint32_t rowbase = tl + uint32_t(tid) * 4u;
+    fill_left_planes(a, rowbase);  // own row only: no barrier needed
+    Acc<KT> acc;
+    acc.init(a.base, a.K);
+    for (int b = 0; b < a.nblocks; ++b) {
+      uint32_t fb;
+      if (streaming) {
+        // release the buffer of block fseq-1, then prefetch block fseq+1 into it
+        __syncthreads();
+        if (warp == 0) {
+          int nb = b + 1;
+          if (nb == a.nblocks) nb = (next < a.ntiles) ? 0 : -1;
+          if (nb >= 0) {
+            if (lane == 0) fence_proxy_async();
+            __syncwarp();
+            issue_block(a, nb, fbuf + ((fseq + 1) & 1) * a.buf_bytes,
+                        bar_f0 + 8u * ((fseq + 1) & 1), lane);
+          }
+        }
+        const bool ok = mbar_wait(bar_f0 + 8u * (fseq & 1), (fseq >> 1) & 1, a.err);
+        if (__syncthreads_or(!ok)) return;
+        fb = fbuf + (fseq & 1) * a.buf_bytes;
+        ++fseq;
+      } else {
+        if (k == 0) {
+          const bool ok = mbar_wait(bar_f0, 0, a.err);
+          if (__syncthreads_or(!ok)) return;
+        }
+        fb = fbuf;
+      }
+      score(fb, b, row, rowbase, acc);
+    }
+    if (row < a.rows) epilogue<KT>(a, acc, row);
+    __syncthreads();  // every thread is done with tile buffer tb
+    if (bulk && a.tile_bufs == 1 && warp == 0 && next < a.ntiles) {
+      if (lane == 0) fence_proxy_async();
+      __syncwarp();
+      issue_tile(a, next, tiles, bar_tile0, lane);
+    }
+  }
+}
+
+}  // namespace dev
+
+// Per-layout launchers (kernels_complete.cu, kernels_explicit.cu).
+cudaError_t launch_complete(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
+                            cudaStream_t stream, int* occupancy_out);
+cudaError_t launch_explicit(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
+                            cudaStream_t stream, int* occupancy_out);
+
+}  // namespace mb

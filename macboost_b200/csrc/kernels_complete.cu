@@ -1,0 +1,131 @@
+// sm_100a forest kernel for the complete (padded-heap) layout.
+//
+// Semantics (per row, bit-exact with the reference CPU predictor,
+// Sources/MacBoost/Booster.swift:2035-2117 and python/macboost/_pyinfer.py:52-89):
+//   acc[c] = baseScores[c];  for t in tree order: acc[t % K] += leaf of t
+// where the walk goes left iff
+//   categorical node : bit `code` of the node mask, code = rint(v) if v finite
+//                      and 0 <= rint(v) < dataBins, else dataBins
+//   NaN              : the node's default direction (flags bit0)
+//   otherwise        : v <= threshold (fp32 compare, no flush-to-zero)
+//
+// Execution model.  One persistent CTA per SM, one thread per row of a row
+// tile of R rows.  The tile's feature columns come from HBM by cp.async.bulk
+// (one copy of R consecutive fp32 values per staged feature, completing on an
+// mbarrier); with two tile buffers the next tile streams in while the current
+// one is scored.  The forest -- or, when larger than shared memory, one block
+// of trees at a time through two buffers -- is staged the same way.  Each
+// thread walks G trees at once (G independent chains of shared-memory loads)
+// and adds their leaves to fp32 accumulators strictly in tree order.
+//
+// The walk keeps the node as a 32-bit shared address o; with heap node n in
+// 8-byte slot n + 1 of a tree whose slots start at A, the child is
+// o' = 2*o - A + 8*go_right, and after D levels the leaf value sits at
+// (o >> 1) + k.  The x gather reads slot row (record.x) at this thread's
+// column: rows of a tile are 4*R bytes apart with R a multiple of 32, so a
+// warp's 32 gathers hit 32 distinct banks whatever features the lanes read,
+// and each heap level of a tree starts on a 128-byte line, so a warp's record
+// loads for one level cost one wavefront (two for the 32-node level of a
+// depth-6 tree).  The kernel is bound by those shared-memory wavefronts and
+// by instruction issue, not by HBM: see the bench's roofline report.
+//
+// Tensor cores are not used: tree traversal is a data-dependent walk, not a
+// dense contraction.  Every mbarrier wait is bounded (globaltimer); on expiry
+// the CTA records kErrWaitTimeout in *err and all its threads return together.
+#include "kernels_common.cuh"
+
+namespace mb {
+namespace {
+
+template <int KT, int G, bool PLANES, bool CAT>
+__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+    forest_complete_kernel(const KArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int D = a.D;
+  const uint32_t NL = 1u << D;          // slots (and leaves) per tree
+  const uint32_t NI = NL - 1;
+  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
+    const int t_block = b * a.Tb;
+    const uint32_t leaves = fb + a.leaf_off;
+    for (int g0 = 0; g0 < a.Tb; g0 += G) {
+      uint32_t A[G], o[G];
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        A[j] = fb + uint32_t(g0 + j) * NL * 8u;
+        o[j] = A[j] + 8u;  // root: heap node 0 in slot 1
+      }
+      for (int L = 0; L < D; ++L) {
+        uint2 r[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const uint32_t right = dev::route<PLANES, CAT>(r[j], rowbase, a.masks, a.data_bins);
+          o[j] = 2u * o[j] - A[j] + (right << 3);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        // heap node n = (o - A)/8 - 1 is leaf n - NI of the tree
+        const uint32_t k = leaves + uint32_t(g0 + j) * NL * 4u - (A[j] >> 1) - 4u - 4u * NI;
+        acc.add(j, t_block + g0 + j, dev::lds_f32((o[j] >> 1) + k));
+      }
+      if (a.out_leaf != nullptr && row < a.rows) {
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const int t = t_block + g0 + j;
+          if (t < a.T) {
+            const uint32_t leaf = (o[j] - A[j]) / 8u - 1u - NI;
+            a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + size_t(t) * NL + leaf);
+          }
+        }
+      }
+    }
+  };
+  dev::run_tiles<KT>(a, smem, score);
+}
+
+using KernelFn = void (*)(const KArgs);
+
+template <int KT, int G>
+KernelFn pick3(bool planes, bool cat) {
+  if (planes)
+    return cat ? forest_complete_kernel<KT, G, true, true>
+               : forest_complete_kernel<KT, G, true, false>;
+  return cat ? forest_complete_kernel<KT, G, false, true>
+             : forest_complete_kernel<KT, G, false, false>;
+}
+
+// (K, G) pairs must match mb::group_options (forest.cpp).
+KernelFn pick(bool planes, bool cat, int K, int G) {
+  switch (K) {
+    case 1: return G == 16 ? pick3<1, 16>(planes, cat) : pick3<1, 8>(planes, cat);
+    case 2: return pick3<2, 8>(planes, cat);
+    case 3: return pick3<3, 6>(planes, cat);
+    case 4: return pick3<4, 8>(planes, cat);
+    case 5: return pick3<5, 5>(planes, cat);
+    case 6: return pick3<6, 6>(planes, cat);
+    case 7: return pick3<7, 7>(planes, cat);
+    case 8: return pick3<8, 8>(planes, cat);
+    case 10: return pick3<10, 10>(planes, cat);
+    case 12: return pick3<12, 12>(planes, cat);
+    case 16: return pick3<16, 16>(planes, cat);
+    default: return pick3<0, 8>(planes, cat);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_complete(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
+                            cudaStream_t stream, int* occupancy_out) {
+  KernelFn fn = pick(planes, cat, a.K, a.G);
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  if (occupancy_out)
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy_out, fn, a.R, smem);
+  fn<<<grid, a.R, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -1,0 +1,102 @@
+// sm_100a forest kernel for the explicit (breadth-first, leaf-record) layout
+// used for deep, sparse trees such as leaf-wise models.  Same semantics,
+// staging pipeline and bounded waits as the complete-layout kernel
+// (kernels_complete.cu); only the walk differs: each record names the
+// distance to its first child, children are adjacent, and a walk ends on a
+// leaf record, so trees of different depths share one loop.
+#include "kernels_common.cuh"
+
+namespace mb {
+namespace {
+
+template <int KT, int G, bool CAT>
+__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+    forest_explicit_kernel(const KArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
+    // block header: [0] trees, [1] first tree index, [4 + i] first record of tree i
+    const int ntrees = int(dev::lds_u32(fb));
+    const int t_block = int(dev::lds_u32(fb + 4u));
+    const uint32_t recs = fb + ((16u + 4u * uint32_t(ntrees) + 15u) & ~15u);
+    for (int g0 = 0; g0 < ntrees; g0 += G) {
+      uint32_t o[G];
+      uint2 r[G];
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        o[j] = recs + 8u * dev::lds_u32(fb + 16u + 4u * uint32_t(g0 + j));
+        r[j] = dev::lds_v2(o[j]);
+      }
+      while (true) {
+        bool any = false;
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          if (r[j].x != kRecLeaf) {
+            // records carry the child distance above the slot offset, so the
+            // slot is always masked; with NaN planes the default-left bit is
+            // clear and the unordered compare applies, as in the planes walk
+            const uint32_t right = dev::route<false, CAT>(r[j], rowbase, a.masks, a.data_bins);
+            o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
+            r[j] = dev::lds_v2(o[j]);
+            any = true;
+          }
+        }
+        if (!any) break;
+      }
+#pragma unroll
+      for (int j = 0; j < G; ++j) acc.add(j, t_block + g0 + j, __uint_as_float(r[j].y));
+      if (a.out_leaf != nullptr && row < a.rows) {
+        const size_t rec_base = a.block_rec_base[b];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const int t = t_block + g0 + j;
+          if (t < a.T)
+            a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + rec_base + (o[j] - recs) / 8u);
+        }
+      }
+    }
+  };
+  dev::run_tiles<KT>(a, smem, score);
+}
+
+using KernelFn = void (*)(const KArgs);
+
+template <int KT, int G>
+KernelFn pick3(bool cat) {
+  return cat ? forest_explicit_kernel<KT, G, true> : forest_explicit_kernel<KT, G, false>;
+}
+
+// (K, G) pairs must match mb::group_options (forest.cpp).  NaN planes need no
+// separate instantiation: explicit records always mask the slot offset and
+// clear the default-left bit when planes are in use.
+KernelFn pick(bool, bool cat, int K, int G) {
+  switch (K) {
+    case 1: return G == 16 ? pick3<1, 16>(cat) : pick3<1, 8>(cat);
+    case 2: return pick3<2, 8>(cat);
+    case 3: return pick3<3, 6>(cat);
+    case 4: return pick3<4, 8>(cat);
+    case 5: return pick3<5, 5>(cat);
+    case 6: return pick3<6, 6>(cat);
+    case 7: return pick3<7, 7>(cat);
+    case 8: return pick3<8, 8>(cat);
+    case 10: return pick3<10, 10>(cat);
+    case 12: return pick3<12, 12>(cat);
+    case 16: return pick3<16, 16>(cat);
+    default: return pick3<0, 8>(cat);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_explicit(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
+                            cudaStream_t stream, int* occupancy_out) {
+  KernelFn fn = pick(planes, cat, a.K, a.G);
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  if (occupancy_out)
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy_out, fn, a.R, smem);
+  fn<<<grid, a.R, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -43,8 +43,9 @@ def test_golden_all_kinds(gpu, tmp_path, name):
     proba = core.predict_ex(h, X, kind=core.KIND_PROBA)
     assert_ulp(proba, g["proba"].astype(np.float32), ULP, f"{name} proba")
     # the reference-signature entry point (feature-major copy, macboost_predict)
-    ref_sig = core.predict(h, X)
-    assert_bitwise(ref_sig.reshape(-1, K), g["pred"], f"{name} macboost_predict")
+    ref_sig = core.predict(h, X).reshape(-1, K)
+    assert_bitwise(ref_sig, pred, f"{name} macboost_predict vs kind=predict")
+    assert_ulp(ref_sig, g["pred"], ULP, f"{name} macboost_predict")
 
 
 CFG_ROWS = {"cfg1": 20_000, "cfg2": 50_000, "cfg3": 20_000, "cfg4": 4_000, "cfg5": 6_000}
