@@ -345,7 +345,7 @@ def main():
                      "traffic": (tr["bytes_per_row"] * rows) if tr else None,
                      "algorithmic_bytes_per_launch": alg_bytes,
                      "note": "algorithmic bytes = rows*4*(used features + output columns); "
-                             "the kernel is node-visit (shared-memory) bound, see DESIGN.md"},
+                             "the tree walk is bound by shared-memory wavefronts, not HBM"},
         "e2e": None if e2e_s is None else {
             "value": units / e2e_s, "unit": UNIT,
             "h2d_bytes_per_step": rows * S * 4, "d2h_bytes_per_step": rows * ocols * 4},
