@@ -140,6 +140,26 @@ uint64_t macboost_kernel_launches(void);
 void *macboost_host_alloc(int64_t bytes);
 void macboost_host_free(void *p);
 
+/* Predict from device memory without allocating any device memory.  No
+ * counterpart in the reference ABI.  For callers that cannot let a library
+ * call cudaMalloc: hosts that reserve (most of) the GPU's memory in their own
+ * pool, where an extra allocation would fail or fragment it, and pipelines
+ * where cudaMalloc/cudaFree would synchronise the device and stall other
+ * streams.  Arguments as macboost_predict_device; the model must already be
+ * resident on `device` (macboost_prepare, done once at set-up, allocates it).
+ * The scratch it needs -- a status word and, for row-major input, a
+ * feature-major copy of x_dev of at most 16 MiB (4,194,304 values,
+ * round_up(rows, 4) * cols) -- is one fixed array inside the library that a
+ * GPU keeps from the first use of this call on it until the process exits;
+ * larger row-major inputs are rejected with an error (split them, or pass
+ * feature-major input, which needs no copy).  Every call shares that array:
+ * calls that overlap on the GPU race, so serialise them.  The first call on a
+ * device looks up the array's address on that device.  The call waits for its
+ * work on `stream` to finish and reports kernel-side errors itself. */
+int32_t macboost_predict_device_noalloc(void *handle, int32_t device, const float *x_dev,
+                                        int64_t rows, int64_t cols, int64_t ld, int32_t layout,
+                                        int32_t kind, void *out_dev, void *stream, char **err);
+
 #ifdef __cplusplus
 }
 #endif

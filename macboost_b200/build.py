@@ -22,7 +22,7 @@ BUILD = PKG / "_build"
 LIB = PKG / "libmacboostc.so"
 
 CXX_SOURCES = ["model.cpp", "forest.cpp", "engine.cpp", "capi.cpp"]
-CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu"]
+CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu", "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

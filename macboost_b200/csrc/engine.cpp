@@ -482,4 +482,41 @@ int engine_check_device(Engine& e, int device, std::string& err) {
   return check_err_word(*d, err);
 }
 
+int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, int64_t ld,
+                           bool use_stage_map, int kind, void* out, unsigned* status,
+                           cudaStream_t stream, std::string& err) {
+  DeviceState* d = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(e.mu);
+    auto it = e.devices.find(device);
+    if (it != e.devices.end()) d = it->second.get();
+  }
+  if (!d) {
+    err = "the model is not resident on device " + std::to_string(device) +
+          ": call macboost_prepare for that device first";
+    return -1;
+  }
+  if (rows <= 0) return 0;
+  DeviceGuard g(device);
+  KArgs a = make_args(e, *d, kind);
+  a.x = x;
+  a.rows = rows;
+  a.ld = ld;
+  a.stage_feature = use_stage_map ? d->stage_feature : nullptr;
+  a.bulk = (reinterpret_cast<uintptr_t>(x) % 16 == 0 && ld % 4 == 0) ? 1 : 0;
+  a.out = kind == kKindLeaf ? nullptr : static_cast<float*>(out);
+  a.out_leaf = kind == kKindLeaf ? static_cast<int*>(out) : nullptr;
+  a.err = status;
+  a.ntiles = (rows + a.R - 1) / a.R;
+  const int grid = int(std::min<int64_t>(a.ntiles, d->grid_ctas));
+  cudaError_t ce = launch_forest(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, a,
+                                 e.flat.plan.smem, grid, stream);
+  if (ce != cudaSuccess) {
+    err = cuda_msg("forest kernel launch", ce);
+    return -1;
+  }
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return 0;
+}
+
 }  // namespace mb

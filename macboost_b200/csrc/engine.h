@@ -77,4 +77,13 @@ int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, i
 // Synchronise `device` and report any kernel-side error since the last check.
 int engine_check_device(Engine& e, int device, std::string& err);
 
+// Enqueue the forest kernel on a device where the model is already resident
+// (engine_prepare ran before), reporting kernel-side errors into the caller's
+// `status` word.  Allocates nothing; fails if the model is not resident.
+// `x` is feature-major with stride ld; `use_stage_map`: x holds every model
+// feature (false: only the staged features, in slot order).
+int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, int64_t ld,
+                           bool use_stage_map, int kind, void* out, unsigned* status,
+                           cudaStream_t stream, std::string& err);
+
 }  // namespace mb
