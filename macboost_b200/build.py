@@ -21,8 +21,9 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libmacboostc.so"
 
-CXX_SOURCES = ["model.cpp", "forest.cpp", "engine.cpp", "capi.cpp"]
-CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu", "noalloc.cu"]
+CXX_SOURCES = ["model.cpp", "forest.cpp", "forest_codes.cpp", "engine.cpp", "capi.cpp"]
+CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu", "kernels_codes.cu",
+              "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

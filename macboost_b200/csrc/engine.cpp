@@ -66,6 +66,9 @@ int ensure(void*& buf, size_t& cap, size_t bytes, std::string& err) {
   return 0;
 }
 
+// Kernel family: 0 complete, 1 explicit, 2 complete with binned codes.
+int layout_code(const FlatForest& f) { return f.codes ? 2 : int(f.layout); }
+
 KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   const FlatForest& f = e.flat;
   KArgs a{};
@@ -88,6 +91,10 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.buf_bytes = f.plan.buf_bytes;
   a.leaf_off = f.leaf_off;
   a.tile_bytes = f.plan.tile_bytes;
+  a.bin_plan = d.bin_plan;
+  a.search = d.search;
+  a.search_depth = f.search_depth;
+  a.code_tile_bytes = f.code_tile_bytes;
   a.data_bins = e.model.num_bins - 1;
   a.kind = kind;
   a.log_link = e.model.uses_log_link() ? 1 : 0;
@@ -116,8 +123,8 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
   }
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = int(std::min<int64_t>(a.ntiles, d.grid_ctas));
-  cudaError_t ce = launch_forest(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, a,
-                                 e.flat.plan.smem, grid, s);
+  cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
+                                 e.flat.plan.smem, grid, s, e.flat.code_bytes);
   if (ce != cudaSuccess) {
     err = cuda_msg("forest kernel launch", ce);
     return -1;
@@ -136,6 +143,7 @@ DeviceState::~DeviceState() {
   for (auto* p : {static_cast<void*>(blob), static_cast<void*>(block_off),
                   static_cast<void*>(block_rec_base), static_cast<void*>(stage_feature),
                   static_cast<void*>(conv_src), static_cast<void*>(conv_dst),
+                  static_cast<void*>(search), static_cast<void*>(bin_plan),
                   static_cast<void*>(masks), static_cast<void*>(leaf_heap),
                   static_cast<void*>(base), static_cast<void*>(err)})
     if (p) cudaFree(p);
@@ -223,7 +231,10 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   if (boff.empty()) boff.push_back(0);
   std::vector<unsigned> rec_base(e.flat.block_rec_base.begin(), e.flat.block_rec_base.end());
   if (rec_base.empty()) rec_base.push_back(0);
-  std::vector<unsigned> masks(e.flat.full_masks.begin(), e.flat.full_masks.end());
+  const std::vector<uint32_t>& mask_src = e.flat.codes ? e.flat.cat_masks : e.flat.full_masks;
+  std::vector<unsigned> masks(mask_src.begin(), mask_src.end());
+  std::vector<float> search(e.flat.search.begin(), e.flat.search.end());
+  std::vector<int> bin_plan(e.flat.bin_plan.begin(), e.flat.bin_plan.end());
   std::vector<int> slots(e.flat.stage_feature.begin(), e.flat.stage_feature.end());
   std::vector<int> csrc(e.flat.conv_src.begin(), e.flat.conv_src.end());
   std::vector<int> cdst(e.flat.conv_dst.begin(), e.flat.conv_dst.end());
@@ -231,6 +242,7 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   if (upload(d->blob, e.flat.blob, err) || upload(d->block_off, boff, err) ||
       upload(d->block_rec_base, rec_base, err) || upload(d->stage_feature, slots, err) ||
       upload(d->conv_src, csrc, err) || upload(d->conv_dst, cdst, err) ||
+      upload(d->search, search, err) || upload(d->bin_plan, bin_plan, err) ||
       upload(d->masks, masks, err) || upload(d->leaf_heap, heap, err) ||
       upload(d->base, base, err))
     return nullptr;
@@ -245,8 +257,8 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
       return nullptr;
     }
   int ctas = 0;
-  ce = forest_occupancy(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, e.flat.K,
-                        e.flat.G, e.flat.plan.R, e.flat.plan.smem, &ctas);
+  ce = forest_occupancy(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, e.flat.K,
+                        e.flat.G, e.flat.plan.R, e.flat.plan.smem, &ctas, e.flat.code_bytes);
   if (ce != cudaSuccess || ctas < 1) {
     err = ce != cudaSuccess ? cuda_msg("occupancy query", ce)
                             : std::string("the forest kernel cannot be resident on an SM");
@@ -509,8 +521,8 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
   a.err = status;
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = int(std::min<int64_t>(a.ntiles, d->grid_ctas));
-  cudaError_t ce = launch_forest(int(e.flat.layout), e.flat.plan.planes, e.model.any_cat, a,
-                                 e.flat.plan.smem, grid, stream);
+  cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
+                                 e.flat.plan.smem, grid, stream, e.flat.code_bytes);
   if (ce != cudaSuccess) {
     err = cuda_msg("forest kernel launch", ce);
     return -1;

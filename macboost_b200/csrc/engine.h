@@ -30,6 +30,8 @@ struct DeviceState {
   int* stage_feature = nullptr;        // staged slot -> feature
   int* conv_src = nullptr;             // -Inf plane fills
   int* conv_dst = nullptr;
+  float* search = nullptr;             // binned codes: threshold search tables
+  int* bin_plan = nullptr;             // binned codes: per staged slot conversions
   unsigned* masks = nullptr;
   int* leaf_heap = nullptr;
   float* base = nullptr;

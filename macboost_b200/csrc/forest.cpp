@@ -35,7 +35,7 @@ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Optional restriction of the planner's choices from the environment, for
 // tuning: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0" (any subset; 0 = free).
 struct PlanOverride {
-  int G = 0, R = 0, bufs = 0, planes = -1;
+  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
     if (!s) return;
@@ -50,6 +50,7 @@ struct PlanOverride {
       else if (key == "R") R = int(v);
       else if (key == "bufs") bufs = int(v);
       else if (key == "planes") planes = int(v);
+      else if (key == "codes") codes = int(v);
       p = end;
       while (*p == ',' || *p == ' ') ++p;
     }
@@ -176,7 +177,27 @@ bool make_blocks(int ngroups, int G, size_t max_block,
 
 }  // namespace
 
+static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int force_planes);
+
 bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_planes) {
+  const PlanOverride ov;
+  FlatForest coded;
+  std::string why;
+  const bool codes_ok = ov.codes != 0 && force_planes != 0 && flatten_codes(m, coded, why, ov.G, ov.R);
+  if (codes_ok && ov.codes == 1) {
+    f = std::move(coded);
+    return true;
+  }
+  if (!flatten_f32(m, f, err, force_planes)) {
+    if (!codes_ok) return false;
+    f = std::move(coded);
+    return true;
+  }
+  if (codes_ok && coded.plan.est_clk_per_row < f.plan.est_clk_per_row) f = std::move(coded);
+  return true;
+}
+
+static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int force_planes) {
   f = FlatForest();
   f.T = int(m.trees.size());
   f.K = m.K;
@@ -230,6 +251,10 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_p
   } best;
   const int Rs[] = {512, 384, 256, 128, 64, 32};
   const PlanOverride ov;
+  if (ov.codes == 1) {
+    err = "binned codes requested but not applicable";
+    return false;
+  }
   if (ov.planes >= 0 && force_planes < 0) force_planes = ov.planes;
   for (int G : group_options(m.K)) {
     if (ov.G && G != ov.G) continue;
@@ -285,8 +310,18 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_p
                 int Tb = 0;
                 for (int t = G; t <= ngroups * G && block_bytes(0, t) <= max_block; t += G) Tb = t;
                 if (Tb == 0) continue;
-                const int nb = (ngroups * G + Tb - 1) / Tb;
-                Tb = int(round_up(size_t((ngroups * G + nb - 1) / nb), size_t(G)));
+                // the block count (>= the minimum) that pads the fewest trees
+                const int nb_min = (ngroups * G + Tb - 1) / Tb;
+                int nb = nb_min, best_pad = 1 << 30;
+                for (int c = nb_min; c <= nb_min + nb_min / 2 + 1; ++c) {
+                  const int tb = ((ngroups + c - 1) / c) * G;
+                  if (block_bytes(0, tb) > max_block) continue;
+                  if (c * tb - f.T < best_pad) {
+                    best_pad = c * tb - f.T;
+                    nb = c;
+                  }
+                }
+                Tb = ((ngroups + nb - 1) / nb) * G;
                 for (int b = 0; b < nb; ++b) blocks.push_back({b * Tb, Tb});
                 p.Tb = Tb;
               } else if (!make_blocks(ngroups, G, max_block, block_bytes, blocks)) {
@@ -323,7 +358,10 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_p
                   ? (double(blocks.size()) * 1500.0 + double(p.buf_bytes) * p.nblocks / 64.0) /
                         double(R)
                   : 0.0;
-          const double cost = (bufs == 2 ? std::max(compute, load) : compute + load) + stream;
+          // a single tile buffer also exposes the bulk-copy latency of each tile
+          const double cost =
+              (bufs == 2 ? std::max(compute, load) : compute + load + 2500.0 / double(R)) +
+              stream;
           p.est_clk_per_row = cost;
           if (cost < best.cost * 0.999) {
             best.p = p;
@@ -481,6 +519,12 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"slots\":" + std::to_string(f.S_stage);
   s += ",\"tile_slots\":" + std::to_string(f.S_total);
   s += ",\"nan_planes\":" + std::string(f.plan.planes ? "true" : "false");
+  s += ",\"codes\":" + std::string(f.codes ? "true" : "false");
+  if (f.codes) {
+    s += ",\"code_bytes\":" + std::to_string(f.code_bytes);
+    s += ",\"code_slots\":" + std::to_string(f.S_code);
+    s += ",\"search_depth\":" + std::to_string(f.search_depth);
+  }
   s += ",\"depth\":" + std::to_string(f.layout == Layout::kComplete ? f.D : f.max_depth);
   s += ",\"rows_per_tile\":" + std::to_string(f.plan.R);
   s += ",\"tile_buffers\":" + std::to_string(f.plan.tile_bufs);

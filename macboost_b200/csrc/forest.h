@@ -124,11 +124,31 @@ struct FlatForest {
   uint32_t leaf_off = 0;               // complete layout: leaves offset in a block
   int max_depth = 0;
   int64_t nodes = 0;
+
+  // Binned-code layout (see forest_codes.cpp): each staged value becomes its
+  // rank among the forest's distinct thresholds of that feature, stored as
+  // code_bytes-wide codes; node records are 4 bytes.
+  bool codes = false;
+  int code_bytes = 1;                  // 1 (u8) or 2 (u16)
+  int S_code = 0;                      // code slots in the tile
+  uint32_t code_tile_bytes = 0;        // bytes of the code tile (after the raw tile)
+  int search_depth = 0;                // d: search tables hold 2^d floats (index 0 unused)
+  std::vector<float> search;           // [tables][2^d] Eytzinger-ordered thresholds
+  std::vector<int32_t> bin_plan;       // [S_stage][4]: table, NaN-right slot, NaN-left slot,
+                                       //               categorical slot (-1: none)
+  std::vector<uint32_t> cat_masks;     // [n][8] masks of categorical nodes
 };
 
 // Flatten a validated model into the device layout and choose a launch plan.
-// `force_planes`: -1 choose, 0 never, 1 always (when it fits).
+// `force_planes`: -1 choose, 0 never, 1 always (when it fits).  The binned-code
+// layout is used when it applies and the planner estimates it faster
+// (MACBOOST_PLAN="codes=0" / "codes=1" restricts the choice).
 bool flatten_forest(const Model& m, FlatForest& out, std::string& err, int force_planes = -1);
+
+// Binned-code flattening of a complete-layout forest; false (with `why`) when
+// the forest does not qualify (too deep, too many distinct thresholds).
+bool flatten_codes(const Model& m, FlatForest& out, std::string& why, int force_G = 0,
+                   int force_R = 0);
 
 // Human-readable JSON description of a flattened forest.
 std::string describe_forest(const FlatForest& f);

@@ -37,6 +37,13 @@ struct KArgs {
   const int* leaf_heap;
   const float* base;                    // [K] starting margins
   int K, G, T, D, Tb, nblocks;      // G: trees walked at once per thread
+  // Binned-code layout: per staged slot {search table, NaN-right code byte
+  // offset, NaN-left code byte offset, categorical code byte offset} (-1: none),
+  // the Eytzinger search tables [tables][2^search_depth], the code tile size.
+  const int* bin_plan;
+  const float* search;
+  int search_depth;
+  unsigned code_tile_bytes;
   unsigned buf_bytes, leaf_off, tile_bytes;
   int data_bins;
   // Output.
@@ -50,14 +57,15 @@ struct KArgs {
   unsigned* err;
 };
 
-// Launch the forest kernel on `stream`.  layout: 0 complete, 1 explicit;
-// planes: NaN planes in the tile; cat: the model has categorical splits.
+// Launch the forest kernel on `stream`.  layout: 0 complete, 1 explicit,
+// 2 complete with binned codes (code_bytes 1 or 2); planes: NaN planes in the
+// tile; cat: the model has categorical splits.
 cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,
-                          int grid, cudaStream_t stream);
+                          int grid, cudaStream_t stream, int code_bytes = 1);
 
 // Largest number of co-resident CTAs per SM for that kernel.
 cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
-                             size_t smem, int* ctas);
+                             size_t smem, int* ctas, int code_bytes = 1);
 
 // Row-major [rows][F] -> feature-major [F][ld] (ld >= rows).
 cudaError_t launch_transpose(const float* in, long long rows, int F, float* out, long long ld,

@@ -213,3 +213,26 @@ def _cudart():
     if _CUDART is None:
         _CUDART = _Cudart()
     return _CUDART
+
+
+@pytest.mark.parametrize("plan", ["codes=0", "codes=0,planes=0", "codes=1", "codes=1,G=8"])
+@pytest.mark.parametrize("cfg", ["cfg1", "cfg2", "cfg3", "cfg4"])
+def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
+    """Each kernel family (fp32 tiles with NaN planes, fp32 with default-left
+    flags, binned codes), forced through MACBOOST_PLAN, against the oracle."""
+    core = gpu
+    if cfg == "cfg4" and "G=8" in plan:
+        pytest.skip("10 classes walk 10 trees per group")
+    monkeypatch.setenv("MACBOOST_PLAN", plan)
+    trees = {"cfg4": 300}.get(cfg)
+    text = synth.model_to_json(synth.make_model(cfg, trees=trees))
+    h = core.load_json(text)
+    desc = json.loads(core.describe(h))
+    assert desc["codes"] == ("codes=1" in plan)
+    if "planes=0" in plan:
+        assert desc["nan_planes"] is False
+    om = O.model_from_dict(json.loads(text))
+    X = synth.make_data(cfg, rows=5003, row_start=999, layout="row")
+    raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"{cfg} {plan} raw")
+    assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"{cfg} {plan}"

@@ -61,7 +61,7 @@ def test_streaming_plan_for_large_forest(lib_built):
     core = lib_built
     m = synth.make_model("cfg4", trees=1000)
     d = json.loads(core.describe(core.load_json(synth.model_to_json(m))))
-    assert d["blocks"] > 1 and d["plan"] == "forest streamed in tree blocks"
+    assert d["blocks"] > 1 and d["plan"].endswith("forest streamed in tree blocks")
     assert d["smem_bytes"] <= 232448
 
 
