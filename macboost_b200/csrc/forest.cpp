@@ -268,7 +268,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
     auto block_bytes = [&](int t0, int n) -> size_t {
       if (complete)
         return round_up(round_up(size_t(n) * NL * 8, 128) + size_t(n) * NL * 4, 128);
-      const size_t head = round_up(16 + 4 * size_t(n), 16);
+      const size_t head = round_up(16 + 4 * size_t(n + n / G), 16);
       return round_up(head + 8 * (node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)]), 128);
     };
     for (int pl = 1; pl >= 0; --pl) {
@@ -277,7 +277,8 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
       if (force_planes == 0 && planes) continue;
       if (force_planes == 1 && !planes && any_left) continue;
       const SlotPlan& sp = planes ? sp_planes : sp_flat;
-      const int S_tile = std::max(sp.S_total, 1);
+      // explicit layout: one more slot holding -Inf, read by leaf records
+      const int S_tile = std::max(sp.S_total, 1) + (complete ? 0 : 1);
       for (int R : Rs) {
         if (R > max_threads_for_group(G) || (ov.R && R != ov.R)) continue;
         for (int bufs = 2; bufs >= 1; --bufs) {
@@ -383,10 +384,11 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
   f.G = best.G;
   const std::vector<std::pair<int, int>>& blocks = best.blocks;
   const std::vector<size_t>& node_prefix = best.node_prefix;
+  const int Gsel = best.G;
   auto block_bytes = [&](int t0, int n) -> size_t {
     if (complete)
       return round_up(round_up(size_t(n) * NL * 8, 128) + size_t(n) * NL * 4, 128);
-    const size_t head = round_up(16 + 4 * size_t(n), 16);
+    const size_t head = round_up(16 + 4 * size_t(n + n / Gsel), 16);
     return round_up(head + 8 * (node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)]), 128);
   };
   const SlotPlan& sp = f.plan.planes ? sp_planes : sp_flat;
@@ -454,13 +456,21 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
   } else {
     f.leaf_heap.assign(node_prefix.back(), -1);
     f.block_rec_base.assign(size_t(nb), 0);
+    // Leaf records loop on themselves: they read the constant -Inf slot (the
+    // tile slot after all staged and -Inf-plane slots) with the default-left
+    // flag, so go_right = (-Inf > leaf value) is 0, and their child distance is
+    // 0; every tree of a group can then take the same number of steps (the
+    // group's deepest leaf) and end on its leaf, whose value is the record's y.
+    const uint32_t leaf_x =
+        uint32_t(std::max(sp.S_total, 1)) * uint32_t(R) * 4u | kRecDefaultLeft;
+    f.neg_inf_slot_bytes = uint32_t(std::max(sp.S_total, 1)) * uint32_t(R) * 4u;
     for (int b = 0; b < nb; ++b) {
       const int t0 = blocks[size_t(b)].first, n = blocks[size_t(b)].second;
       uint8_t* blk = f.blob.data() + f.block_off[size_t(b)];
       auto* head = reinterpret_cast<uint32_t*>(blk);
       head[0] = uint32_t(n);
       head[1] = uint32_t(t0);
-      const size_t rec_off = round_up(16 + 4 * size_t(n), 16);
+      const size_t rec_off = round_up(16 + 4 * size_t(n + n / Gsel), 16);
       auto* recs = reinterpret_cast<uint2_like*>(blk + rec_off);
       const size_t base = node_prefix[size_t(t0)];
       f.block_rec_base[size_t(b)] = uint32_t(base);
@@ -470,11 +480,14 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
         head[4 + i] = start;
         uint2_like* r = recs + start;
         int32_t* heap = f.leaf_heap.data() + node_prefix[size_t(t)];
+        uint32_t& steps = head[4 + n + i / Gsel];  // per group: its deepest leaf
+        if (i % Gsel == 0) steps = 0;
         if (t >= f.T) {
-          r[0] = uint2_like{kRecLeaf, nz_bits};
+          r[0] = uint2_like{leaf_x, nz_bits};
           continue;
         }
         const Tree& tr = m.trees[size_t(t)];
+        steps = std::max<uint32_t>(steps, uint32_t(tr.depth));
         std::vector<int64_t> order{0};
         uint32_t next = 1;
         for (size_t q = 0; q < order.size(); ++q) {
@@ -482,7 +495,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
           if (tr.feature[size_t(o)] < 0) {
             uint32_t bits;
             std::memcpy(&bits, &tr.leaf[size_t(o)], 4);
-            r[q] = uint2_like{kRecLeaf, bits};
+            r[q] = uint2_like{leaf_x, bits};
             heap[q] = int32_t(o);
             continue;
           }

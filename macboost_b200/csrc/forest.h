@@ -30,9 +30,12 @@
 //
 // EXPLICIT layout (deeper, sparse trees such as leaf-wise models).  The
 // reachable nodes of each tree are stored breadth-first with both children of
-// a node adjacent, so child = first_child + go_right.  A block holds
-//   header [4 + Tb]  uint32  [0] trees, [1] first tree index, [4 + i] first
-//                            record of tree i (padded to 16 bytes)
+// a node adjacent, so child = first_child + go_right.  Leaf records loop on
+// themselves, so all trees of a group walk the same number of steps.  A block
+// holds
+//   header [4 + Tb + Tb/G]  uint32  [0] trees, [1] first tree index, [4 + i]
+//                            first record of tree i, [4 + Tb + g] steps of
+//                            group g (padded to 16 bytes)
 //   records [...]    uint2
 // and blocks are variable-sized (block_off[] gives their byte offsets).
 //
@@ -43,7 +46,8 @@
 //                       bit2: categorical split with a full 256-bit mask
 //   x bits 7..17 byte offset of the slot row in the tile (a multiple of 4*R)
 //   x bits 18..31 explicit layout: index distance to the first child
-//   x == 0xFFFFFFFF explicit layout: leaf (y = leaf value bits)
+//   explicit-layout leaf: x = the -Inf slot | bit0, child distance 0,
+//                         y = leaf value bits
 //   y            float bits of the threshold (numeric),
 //                mask bits 0..31 (categorical, bits 32..dataBins uniform),
 //                or the index of the node's 8-word mask (full mask).
@@ -69,7 +73,6 @@ constexpr uint32_t kRecDefaultLeft = 1u;
 constexpr uint32_t kRecCategorical = 2u;
 constexpr uint32_t kRecFullMask = 4u;
 constexpr uint32_t kRecSlotMask = 0x3FF80u;   // bits 7..17
-constexpr uint32_t kRecLeaf = 0xFFFFFFFFu;    // explicit-layout leaf marker
 constexpr int kRecChildShift = 18;
 constexpr uint32_t kMaxChildDelta = 16383u;
 
@@ -124,6 +127,7 @@ struct FlatForest {
   uint32_t leaf_off = 0;               // complete layout: leaves offset in a block
   int max_depth = 0;
   int64_t nodes = 0;
+  uint32_t neg_inf_slot_bytes = 0xFFFFFFFFu;  // explicit: tile offset of the -Inf slot
 
   // Binned-code layout (see forest_codes.cpp): each staged value becomes its
   // rank among the forest's distinct thresholds of that feature, stored as

@@ -44,6 +44,7 @@ struct KArgs {
   const float* search;
   int search_depth;
   unsigned code_tile_bytes;
+  unsigned neg_inf_slot;           // explicit layout: tile offset of the constant -Inf slot
   unsigned buf_bytes, leaf_off, tile_bytes;
   int data_bins;
   // Output.

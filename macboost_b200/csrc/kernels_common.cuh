@@ -251,6 +251,12 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
     for (int i = 0; i < 4; ++i) mbar_init(base + 8u * i, 1);
     fence_mbar_init();
   }
+  if (a.neg_inf_slot != 0xFFFFFFFFu) {
+    // constant -Inf slot read by explicit-layout leaf records; no copy writes it
+    for (int b = 0; b < a.tile_bufs; ++b)
+      sts_f32(tiles + uint32_t(b) * a.tile_bytes + a.neg_inf_slot + uint32_t(tid) * 4u,
+              -__int_as_float(0x7f800000));
+  }
   __syncthreads();
 
   long long tile = blockIdx.x;

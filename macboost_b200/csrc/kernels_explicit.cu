@@ -2,8 +2,9 @@
 // used for deep, sparse trees such as leaf-wise models.  Same semantics,
 // staging pipeline and bounded waits as the complete-layout kernel
 // (kernels_complete.cu); only the walk differs: each record names the
-// distance to its first child, children are adjacent, and a walk ends on a
-// leaf record, so trees of different depths share one loop.
+// distance to its first child, children are adjacent, and leaf records loop on
+// themselves, so the G trees of a group all take the group's step count (its
+// deepest leaf) without per-step branches and end on their leaves.
 #include "kernels_common.cuh"
 
 namespace mb {
@@ -14,36 +15,33 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
     forest_explicit_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
-    // block header: [0] trees, [1] first tree index, [4 + i] first record of tree i
+    // block header: [0] trees, [1] first tree index, [4 + i] first record of
+    // tree i, [4 + trees + g] steps of group g
     const int ntrees = int(dev::lds_u32(fb));
     const int t_block = int(dev::lds_u32(fb + 4u));
-    const uint32_t recs = fb + ((16u + 4u * uint32_t(ntrees) + 15u) & ~15u);
+    const uint32_t steps_at = fb + 16u + 4u * uint32_t(ntrees);
+    const uint32_t recs =
+        fb + ((16u + 4u * uint32_t(ntrees + ntrees / G) + 15u) & ~15u);
     for (int g0 = 0; g0 < ntrees; g0 += G) {
+      const int steps = int(dev::lds_u32(steps_at + 4u * uint32_t(g0 / G)));
       uint32_t o[G];
-      uint2 r[G];
 #pragma unroll
-      for (int j = 0; j < G; ++j) {
-        o[j] = recs + 8u * dev::lds_u32(fb + 16u + 4u * uint32_t(g0 + j));
-        r[j] = dev::lds_v2(o[j]);
-      }
-      while (true) {
-        bool any = false;
+      for (int j = 0; j < G; ++j) o[j] = recs + 8u * dev::lds_u32(fb + 16u + 4u * uint32_t(g0 + j));
+      for (int it = 0; it < steps; ++it) {
+        uint2 r[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
 #pragma unroll
         for (int j = 0; j < G; ++j) {
-          if (r[j].x != kRecLeaf) {
-            // records carry the child distance above the slot offset, so the
-            // slot is always masked; with NaN planes the default-left bit is
-            // clear and the unordered compare applies, as in the planes walk
-            const uint32_t right = dev::route<false, CAT>(r[j], rowbase, a.masks, a.data_bins);
-            o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
-            r[j] = dev::lds_v2(o[j]);
-            any = true;
-          }
+          // records carry the child distance above the slot offset, so the
+          // slot is always masked; leaves read the -Inf slot with the
+          // default-left bit (go_right = 0) and have distance 0: they stay put
+          const uint32_t right = dev::route<false, CAT>(r[j], rowbase, a.masks, a.data_bins);
+          o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
         }
-        if (!any) break;
       }
 #pragma unroll
-      for (int j = 0; j < G; ++j) acc.add(j, t_block + g0 + j, __uint_as_float(r[j].y));
+      for (int j = 0; j < G; ++j) acc.add(j, t_block + g0 + j, dev::lds_f32(o[j] + 4u));
       if (a.out_leaf != nullptr && row < a.rows) {
         const size_t rec_base = a.block_rec_base[b];
 #pragma unroll
