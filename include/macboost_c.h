@@ -90,7 +90,10 @@ enum {
   MACBOOST_KIND_PROBA = 2,   /* predict_proba (__init__.py:433-445): rows x 2 [1-p, p] for
                                 one class, softmax rows x K otherwise; evaluated in float64,
                                 rounded to float32 */
-  MACBOOST_KIND_LEAF = 3     /* int32 heap index of the leaf reached, rows x num_trees */
+  MACBOOST_KIND_LEAF = 3,    /* int32 heap index of the leaf reached, rows x num_trees */
+  MACBOOST_KIND_CLI = 4      /* what `macboost predict` writes (MacBoostCLI/main.swift:344-364):
+                                float32 softmax for K > 1, sigmoid for the binary objective,
+                                else MACBOOST_KIND_PREDICT; rows x K */
 };
 enum { MACBOOST_LAYOUT_FEATURE_MAJOR = 0, MACBOOST_LAYOUT_ROW_MAJOR = 1 };
 

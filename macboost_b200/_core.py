@@ -18,7 +18,7 @@ from pathlib import Path
 
 import numpy as np
 
-KIND_PREDICT, KIND_RAW, KIND_PROBA, KIND_LEAF = 0, 1, 2, 3
+KIND_PREDICT, KIND_RAW, KIND_PROBA, KIND_LEAF, KIND_CLI = 0, 1, 2, 3, 4
 LAYOUT_FEATURE_MAJOR, LAYOUT_ROW_MAJOR = 0, 1
 
 _PKG = Path(__file__).resolve().parent

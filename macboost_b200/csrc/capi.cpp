@@ -165,7 +165,7 @@ int64_t macboost_best_iteration(void* handle) { return handle ? 0 : -1; }
 char* macboost_warnings(void* /*handle*/) { return nullptr; }
 
 int64_t macboost_output_cols(void* handle, int32_t kind) {
-  if (!handle || kind < mb::kKindPredict || kind > mb::kKindLeaf) return -1;
+  if (!handle || kind < mb::kKindPredict || kind > mb::kKindCli) return -1;
   return mb::output_cols(*engine(handle), kind);
 }
 

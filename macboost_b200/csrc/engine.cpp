@@ -99,6 +99,7 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.data_bins = e.model.num_bins - 1;
   a.kind = kind;
   a.log_link = e.model.uses_log_link() ? 1 : 0;
+  a.binary = e.model.objective == kBinaryLogistic ? 1 : 0;
   a.R = f.plan.R;
   a.tile_bufs = f.plan.tile_bufs;
   a.err = d.err;
@@ -390,7 +391,7 @@ int engine_predict_host(Engine& e, const float* x, int64_t rows, int64_t cols, i
     err = "layout must be 0 (feature-major) or 1 (row-major)";
     return -1;
   }
-  if (kind < kKindPredict || kind > kKindLeaf) {
+  if (kind < kKindPredict || kind > kKindCli) {
     err = "unknown output kind " + std::to_string(kind);
     return -1;
   }
@@ -453,7 +454,7 @@ int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, i
           std::to_string(cols);
     return -1;
   }
-  if (kind < kKindPredict || kind > kKindLeaf) {
+  if (kind < kKindPredict || kind > kKindCli) {
     err = "unknown output kind " + std::to_string(kind);
     return -1;
   }

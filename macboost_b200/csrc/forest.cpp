@@ -26,7 +26,7 @@ std::vector<int> group_options(int K) {
   }
 }
 
-int max_threads_for_group(int G) { return G >= 12 ? 256 : 512; }
+int max_threads_for_group(int G) { return G >= 12 ? 256 : (G >= 10 ? 512 : 640); }
 
 namespace {
 
@@ -249,7 +249,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
     std::vector<size_t> node_prefix;
     double cost = 1e300;
   } best;
-  const int Rs[] = {512, 384, 256, 128, 64, 32};
+  const int Rs[] = {640, 512, 384, 256, 128, 64, 32};
   const PlanOverride ov;
   if (ov.codes == 1) {
     err = "binned codes requested but not applicable";

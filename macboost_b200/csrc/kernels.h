@@ -14,6 +14,7 @@ enum Kind : int {
   kKindRaw = 1,      // raw margins
   kKindProba = 2,    // predict_proba: sigmoid [1-p, p] (K == 1) or softmax (K > 1), float64 math
   kKindLeaf = 3,     // leaf heap index per (row, tree), int32
+  kKindCli = 4,      // what `macboost predict` writes: fp32 softmax (K > 1) / sigmoid (binary)
 };
 
 // Kernel error bits (written to KArgs::err).
@@ -50,6 +51,7 @@ struct KArgs {
   // Output.
   int kind;
   int log_link;
+  int binary;                      // objective is binary logistic (kKindCli sigmoid)
   float* out;                      // float output (kinds 0-2) or null
   int* out_leaf;                   // leaf output (kind 3) or null
   // Launch plan.

@@ -18,7 +18,7 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 // need the larger per-thread register budget (mb::max_threads_for_group).
 template <int G>
 struct Bounds {
-  static constexpr int kMaxThreads = G >= 12 ? 256 : 512;
+  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 ? 512 : 640);
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -219,6 +219,32 @@ __device__ __forceinline__ void epilogue(const KArgs& a, const Acc<KT>& acc, lon
       double s = 0.0;
       for (int c = 0; c < K; ++c) s += exp(double(acc.get(c)) - m);
       for (int c = 0; c < K; ++c) o[row * K + c] = float(exp(double(acc.get(c)) - m) / s);
+    }
+    return;
+  }
+  if (a.kind == kKindCli) {
+    // Sources/MacBoostCLI/main.swift:344-364, in float32: predict (exp for
+    // log-link objectives), then a softmax over classes (max-shifted, class-
+    // order sum, divide) when K > 1, or 1 / (1 + exp(-x)) for the binary
+    // objective.  exp is evaluated as the float32 rounding of the float64 exp.
+    float v[KT == 0 ? 128 : KT];
+    for (int c = 0; c < K; ++c) {
+      v[c] = acc.get(c);
+      if (a.log_link) v[c] = float(exp(double(v[c])));
+    }
+    if (K > 1) {
+      float mx = -__int_as_float(0x7f800000);
+      for (int c = 0; c < K; ++c) mx = v[c] > mx ? v[c] : mx;
+      float sum = 0.0f;
+      for (int c = 0; c < K; ++c) {
+        v[c] = float(exp(double(v[c] - mx)));
+        sum += v[c];
+      }
+      for (int c = 0; c < K; ++c) o[row * K + c] = v[c] / sum;
+    } else if (a.binary) {
+      o[row] = 1.0f / (1.0f + float(exp(double(-v[0]))));
+    } else {
+      o[row] = v[0];
     }
     return;
   }

@@ -43,7 +43,6 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
   extern __shared__ __align__(128) unsigned char smem[];
   const int D = a.D;
   const uint32_t NL = 1u << D;          // slots (and leaves) per tree
-  const uint32_t NI = NL - 1;
   auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
     const int t_block = b * a.Tb;
     const uint32_t leaves = fb + a.leaf_off;
@@ -66,8 +65,8 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
       }
 #pragma unroll
       for (int j = 0; j < G; ++j) {
-        // heap node n = (o - A)/8 - 1 is leaf n - NI of the tree
-        const uint32_t k = leaves + uint32_t(g0 + j) * NL * 4u - (A[j] >> 1) - 4u - 4u * NI;
+        // heap node n = (o - A)/8 - 1 is leaf n - (NL - 1) of the tree
+        const uint32_t k = leaves + uint32_t(g0 + j) * NL * 4u - (A[j] >> 1) - 4u * NL;
         acc.add(j, t_block + g0 + j, dev::lds_f32((o[j] >> 1) + k));
       }
       if (a.out_leaf != nullptr && row < a.rows) {
@@ -75,7 +74,7 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
         for (int j = 0; j < G; ++j) {
           const int t = t_block + g0 + j;
           if (t < a.T) {
-            const uint32_t leaf = (o[j] - A[j]) / 8u - 1u - NI;
+            const uint32_t leaf = (o[j] - A[j]) / 8u - NL;
             a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + size_t(t) * NL + leaf);
           }
         }

@@ -81,7 +81,7 @@ extern "C" __attribute__((visibility("default"))) int32_t macboost_predict_devic
                        " features, got " + std::to_string(cols));
     return -1;
   }
-  if (kind < mb::kKindPredict || kind > mb::kKindLeaf) {
+  if (kind < mb::kKindPredict || kind > mb::kKindCli) {
     set_error(err, "unknown output kind " + std::to_string(kind));
     return -1;
   }

@@ -167,6 +167,34 @@ def predict(model: OracleModel, raw: np.ndarray) -> np.ndarray:
     return raw
 
 
+def predict_cli(model: OracleModel, raw: np.ndarray) -> np.ndarray:
+    """What `macboost predict` writes (Sources/MacBoostCLI/main.swift:344-364),
+    in float32: `predict` (exp for log-link objectives), then per row a softmax
+    (max-shifted, class-order float32 sum, divide) when K > 1, or
+    1 / (1 + exp(-x)) for the binary objective.  exp is the float32 rounding
+    of the float64 exp (a correctly rounded expf)."""
+    def exp32(x):
+        return np.exp(np.asarray(x, dtype=np.float64)).astype(np.float32)
+
+    v = np.asarray(raw, dtype=np.float32).reshape(raw.shape[0], -1).copy()
+    if model.objective in LOG_LINK_OBJECTIVES:
+        v = exp32(v)
+    K = v.shape[1]
+    if K > 1:
+        mx = np.full(v.shape[0], -np.inf, dtype=np.float32)
+        for c in range(K):
+            mx = np.where(v[:, c] > mx, v[:, c], mx)
+        s = np.zeros(v.shape[0], dtype=np.float32)
+        for c in range(K):
+            v[:, c] = exp32(v[:, c] - mx)
+            s = (s + v[:, c]).astype(np.float32)
+        return (v / s[:, None]).astype(np.float32)
+    if model.objective == 1:
+        one = np.float32(1.0)
+        return (one / (one + exp32(-v))).astype(np.float32)
+    return v
+
+
 def predict_proba(raw: np.ndarray) -> np.ndarray:
     """MacBoostClassifier.predict_proba formula (__init__.py:439-445), float64."""
     raw = np.asarray(raw).astype(np.float64)

@@ -236,3 +236,16 @@ def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
     raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
     assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"{cfg} {plan} raw")
     assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"{cfg} {plan}"
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_cli_transform_kind(gpu, oracle_built, name):
+    """MACBOOST_KIND_CLI: the float32 transform `macboost predict` applies."""
+    core = gpu
+    g = golden_arrays(name)
+    h = core.load_json(golden_text(name))
+    m = golden_oracle_model(name)
+    with np.errstate(over="ignore"):
+        ref = O.predict_cli(m, g["raw"])
+    got = core.predict_ex(h, g["X"], kind=core.KIND_CLI)
+    assert_ulp(got, ref, ULP, f"{name} cli transform")
