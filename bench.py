@@ -85,60 +85,122 @@ class Dist:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms."""
+    """SM clocks and clock-event (throttle) reasons during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NVML, read by a thread every 5 ms, plus `sample()` calls that the timed
+    loop makes while its queued launches are still running, so that even a
+    region of a few milliseconds holds samples.  Falls back to nvidia-smi
+    (50 ms) when NVML cannot be opened."""
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4))
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
         self.device = device
+        self.samples = []          # (sm MHz, set of reasons)
+        self.max_mhz = None
+        self.nvml = None
+        self.handle = None
         self.proc = None
         self.lines = []
+        self.running = False
+        self.lock = threading.Lock()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = self._nvml_handle(device)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle,
+                                                                 pynvml.NVML_CLOCK_SM))
+            self._reason_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) \
+                or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            self.nvml = None
+
+    def _nvml_handle(self, device):
+        pynvml = self.nvml
+        try:
+            import torch
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(device)
+
+    def sample(self):
+        if self.nvml is None:
+            return
+        try:
+            mhz = float(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+            mask = int(self._reason_fn(self.handle))
+        except Exception:
+            return
+        active = {name for name, attr, bit in self.REASONS
+                  if mask & int(getattr(self.nvml, attr, bit))}
+        with self.lock:
+            self.samples.append((mhz, active))
+
+    def _loop(self):
+        while self.running:
+            self.sample()
+            time.sleep(0.005)
 
     def start(self):
+        if self.nvml is not None:
+            self.running = True
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50", "-i", str(self.device)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict | None:
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.thread.join(timeout=2)
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
+        if self.nvml is not None:
+            self.running = False
+            self.thread.join(timeout=2)
+        elif self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+            for ln in self.lines:
+                parts = [p.strip() for p in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    mhz = float(parts[1])
+                    self.max_mhz = float(parts[2])
+                except ValueError:
+                    continue
+                active = {name for (name, _, _), v in zip(self.REASONS, parts[5:9])
+                          if v.lower().startswith("active")}
+                self.samples.append((mhz, active))
+        else:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return None
+        reasons = set().union(*(r for _, r in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
 def traffic_lookup(cfg: str):
@@ -299,6 +361,7 @@ def main():
     for _ in range(args.steps):
         step()
     ev1.record(stream)
+    clocks.sample()            # the queued steps are running now
     torch.cuda.synchronize(dev)
     dist.barrier()
     launches = _core.kernel_launches() - launches0

@@ -163,6 +163,65 @@ int32_t macboost_predict_device_noalloc(void *handle, int32_t device, const floa
                                         int64_t rows, int64_t cols, int64_t ld, int32_t layout,
                                         int32_t kind, void *out_dev, void *stream, char **err);
 
+/* ---- text input and the `macboost predict` command (additive) ----------- */
+
+/* Feature names stored in the model file (`featureNames`, Booster.swift:2126,
+ * 2158): their count, or -1 when the file has none / for a NULL handle; and
+ * name i (owned by the handle, NULL when out of range). */
+int64_t macboost_num_feature_names(void *handle);
+const char *macboost_feature_name(void *handle, int64_t i);
+
+enum { MACBOOST_FORMAT_CSV = 0, MACBOOST_FORMAT_LIBSVM = 1, MACBOOST_FORMAT_AUTO = 2 };
+
+/* Read a text table into host memory with the rules of MacBoost's CLI
+ * readers.  MACBOOST_FORMAT_CSV replaces CSV.read (Sources/MacBoostCLI/
+ * CSV.swift:48-118): a header row, tab-delimited when the header holds a tab
+ * else comma-delimited, names trimmed of white space; blank lines and lines
+ * starting with '\r' skipped; each field read with strtof in place, empty or
+ * non-numeric fields NaN; extra fields ignored; a row with fewer fields than
+ * the header fails ("Malformed CSV: row N has fewer fields than the header
+ * (C)", N the first such data row, from 1).  MACBOOST_FORMAT_LIBSVM replaces
+ * CSV.readLibSVM (CSV.swift:126-217): "label idx:value ..." lines, '#'
+ * comments, non-"idx:" tokens (qid:...) skipped, 0- or 1-based indices
+ * detected from the smallest index, absent features 0, columns named
+ * label,f0,f1,...; a negative index fails.  MACBOOST_FORMAT_AUTO picks LibSVM
+ * for the .svm / .libsvm extensions (MacBoostCLI/main.swift:98-110).
+ * Returns a table handle (release with macboost_table_free) or NULL. */
+void *macboost_table_read(const char *path, int32_t format, char **err);
+int64_t macboost_table_rows(void *table);
+int64_t macboost_table_cols(void *table);
+/* Name of column `col` (owned by the table; NULL when out of range). */
+const char *macboost_table_column_name(void *table, int64_t col);
+/* The values, row-major rows x cols float32 (owned by the table). */
+const float *macboost_table_data(void *table);
+void macboost_table_free(void *table);
+
+/* Write a prediction file as the CLI does: CSV.writePredictions
+ * (CSV.swift:219-224) for k == 1 (header "prediction", one value per line),
+ * else the multiclass branch of runPredict (main.swift:357-361, header
+ * class_0,...,class_{k-1}, one comma-separated row per line).  Values are
+ * printed as Swift prints a Float: shortest round-trip digits, exponent form
+ * ("1e-05", "1.2345679e+08") below 1e-4 or above 2^24, else positional with
+ * at least one fractional digit ("1.0", "0.25"); "nan", "inf", "-inf".
+ * The file is written beside `path` and renamed over it. */
+int32_t macboost_write_predictions(const float *preds, int64_t rows, int64_t k, const char *path,
+                                   char **err);
+
+/* `macboost predict --model M --data D --output O [--raw]`: replaces runPredict,
+ * MacBoostCLI/main.swift:317-371, on this engine.  Reads `data_path`
+ * (`format` as macboost_table_read; the reference reads CSV/TSV), maps the
+ * model's features to columns by name when the model stores names, else takes
+ * the first num_features columns; predicts on devices[0..ndev) (ndev == 0:
+ * MACBOOST_DEVICES, else the current device); writes MACBOOST_KIND_CLI
+ * output, or MACBOOST_KIND_PREDICT when `raw` is non-zero, to `output_path`
+ * with macboost_write_predictions; stores the row count in *rows_out.  Errors
+ * use the reference's messages ("Malformed CSV: column 'x' required by the
+ * model is missing", "model expects N features, CSV has C columns", the
+ * reader's), reported after the whole file has been read. */
+int32_t macboost_cli_predict(void *handle, const char *data_path, int32_t format, int32_t raw,
+                             const int32_t *devices, int32_t ndev, const char *output_path,
+                             int64_t *rows_out, char **err);
+
 #ifdef __cplusplus
 }
 #endif

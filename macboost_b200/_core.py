@@ -20,6 +20,7 @@ import numpy as np
 
 KIND_PREDICT, KIND_RAW, KIND_PROBA, KIND_LEAF, KIND_CLI = 0, 1, 2, 3, 4
 LAYOUT_FEATURE_MAJOR, LAYOUT_ROW_MAJOR = 0, 1
+FORMATS = {"csv": 0, "tsv": 0, "libsvm": 1, "auto": 2}
 
 _PKG = Path(__file__).resolve().parent
 
@@ -68,6 +69,17 @@ def _configure(lib):
         "macboost_kernel_launches": (ctypes.c_uint64, []),
         "macboost_host_alloc": (P, [I64]),
         "macboost_host_free": (None, [P]),
+        "macboost_num_feature_names": (I64, [P]),
+        "macboost_feature_name": (ctypes.c_char_p, [P, I64]),
+        "macboost_table_read": (P, [ctypes.c_char_p, I32, _c_char_pp]),
+        "macboost_table_rows": (I64, [P]),
+        "macboost_table_cols": (I64, [P]),
+        "macboost_table_column_name": (ctypes.c_char_p, [P, I64]),
+        "macboost_table_data": (P, [P]),
+        "macboost_table_free": (None, [P]),
+        "macboost_write_predictions": (I32, [P, I64, I64, ctypes.c_char_p, _c_char_pp]),
+        "macboost_cli_predict": (I32, [P, ctypes.c_char_p, I32, I32, _i32_p, I32,
+                                       ctypes.c_char_p, ctypes.POINTER(I64), _c_char_pp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -294,3 +306,65 @@ def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
     arr = np.frombuffer(buf, dtype=dtype, count=int(np.prod(shape))).reshape(shape)
     weakref.finalize(buf, _lib.macboost_host_free, ptr)
     return arr
+
+
+def feature_names(handle: _Handle) -> list[str] | None:
+    """The model file's `featureNames`, or None when it has none."""
+    n = _lib.macboost_num_feature_names(handle.ptr)
+    if n < 0:
+        return None
+    return [_lib.macboost_feature_name(handle.ptr, i).decode() for i in range(n)]
+
+
+def _format_code(fmt: str) -> int:
+    try:
+        return FORMATS[fmt]
+    except KeyError:
+        raise ValueError(f"unknown format {fmt!r} (csv | tsv | libsvm | auto)") from None
+
+
+def read_table(path, fmt: str = "csv") -> tuple[list[str], np.ndarray]:
+    """A CSV / TSV / LibSVM file read with the CLI's rules: (column names,
+    float32 (rows, cols) row-major copy)."""
+    err = ctypes.c_char_p()
+    t = _lib.macboost_table_read(str(path).encode(), _format_code(fmt), ctypes.byref(err))
+    if not t:
+        raise MacBoostError(_take_error(err))
+    try:
+        rows = _lib.macboost_table_rows(t)
+        cols = _lib.macboost_table_cols(t)
+        names = [_lib.macboost_table_column_name(t, c).decode() for c in range(cols)]
+        out = np.empty((rows, cols), dtype=np.float32)
+        if out.size:
+            ctypes.memmove(out.ctypes.data, _lib.macboost_table_data(t), out.nbytes)
+        return names, out
+    finally:
+        _lib.macboost_table_free(t)
+
+
+def write_predictions(preds, path) -> None:
+    """The CLI's prediction file for (rows,) or (rows, k) float32 values."""
+    p = np.ascontiguousarray(preds, dtype=np.float32)
+    rows = p.shape[0]
+    k = 1 if p.ndim == 1 else int(np.prod(p.shape[1:]))
+    err = ctypes.c_char_p()
+    if _lib.macboost_write_predictions(p.ctypes.data if p.size else None, rows, max(k, 1),
+                                       str(path).encode(), ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+
+
+def cli_predict(handle: _Handle, data_path, output_path, fmt: str = "csv", raw: bool = False,
+                devices=None) -> int:
+    """`macboost predict` on an open model: returns the rows written."""
+    devs = None
+    nd = 0
+    if devices:
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        nd = len(devices)
+    rows = ctypes.c_int64(0)
+    err = ctypes.c_char_p()
+    if _lib.macboost_cli_predict(handle.ptr, str(data_path).encode(), _format_code(fmt),
+                                 1 if raw else 0, devs, nd, str(output_path).encode(),
+                                 ctypes.byref(rows), ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+    return rows.value

@@ -20,8 +20,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libmacboostc.so"
+CLI = PKG / "macboost"          # the `macboost` command (C++ over the C ABI)
 
-CXX_SOURCES = ["model.cpp", "forest.cpp", "forest_codes.cpp", "engine.cpp", "capi.cpp"]
+CXX_SOURCES = ["model.cpp", "forest.cpp", "forest_codes.cpp", "engine.cpp", "table.cpp",
+               "capi.cpp"]
 CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu", "kernels_codes.cu",
               "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -44,10 +46,10 @@ def _sources():
 
 
 def needs_build() -> bool:
-    if not LIB.exists():
+    if not LIB.exists() or not CLI.exists():
         return True
-    t = LIB.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in _sources())
+    t = min(LIB.stat().st_mtime, CLI.stat().st_mtime)
+    return any(p.stat().st_mtime > t for p in _sources() + [CSRC / "cli_main.cpp"])
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -93,7 +95,22 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         sys.stdout.write(r.stdout)
         raise RuntimeError("link failed: " + " ".join(link))
     os.replace(tmp, LIB)
+    build_cli(cxx)
     return LIB
+
+
+def build_cli(cxx: str = "g++") -> Path:
+    """The `macboost` executable: main.swift's inference commands in C++,
+    linked to libmacboostc.so beside it (rpath $ORIGIN)."""
+    tmp = CLI.with_name(f"macboost.tmp{os.getpid()}")
+    cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-Wextra", str(CSRC / "cli_main.cpp"),
+           "-o", str(tmp), f"-L{PKG}", "-lmacboostc", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if r.returncode:
+        sys.stdout.write(r.stdout)
+        raise RuntimeError("CLI build failed: " + " ".join(cmd))
+    os.replace(tmp, CLI)
+    return CLI
 
 
 if __name__ == "__main__":

@@ -7,11 +7,13 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <new>
 #include <string>
 #include <vector>
 
 #include "../../include/macboost_c.h"
 #include "engine.h"
+#include "table.h"
 
 namespace {
 
@@ -264,6 +266,87 @@ int32_t macboost_select_features(const char*, const float*, int64_t, int64_t, co
 int32_t macboost_predict_contrib(void*, const float*, int64_t, int64_t, float*, char** err) {
   set_error(err, std::string("SHAP contributions are ") + kNoTraining);
   return -1;
+}
+
+int64_t macboost_num_feature_names(void* handle) {
+  if (!handle) return -1;
+  const mb::Model& m = engine(handle)->model;
+  return m.has_feature_names ? int64_t(m.feature_names.size()) : -1;
+}
+
+const char* macboost_feature_name(void* handle, int64_t i) {
+  if (!handle) return nullptr;
+  const mb::Model& m = engine(handle)->model;
+  if (!m.has_feature_names || i < 0 || i >= int64_t(m.feature_names.size())) return nullptr;
+  return m.feature_names[size_t(i)].c_str();
+}
+
+void* macboost_table_read(const char* path, int32_t format, char** err) {
+  if (!path) {
+    set_error(err, "null path");
+    return nullptr;
+  }
+  auto* t = new (std::nothrow) mb::Table();
+  if (!t) {
+    set_error(err, "out of host memory");
+    return nullptr;
+  }
+  std::string e;
+  if (!mb::read_table(path, format, mb::ColumnChooser(), false, *t, e)) {
+    delete t;
+    set_error(err, e);
+    return nullptr;
+  }
+  return t;
+}
+
+int64_t macboost_table_rows(void* table) {
+  return table ? static_cast<mb::Table*>(table)->rows : -1;
+}
+
+int64_t macboost_table_cols(void* table) {
+  return table ? static_cast<mb::Table*>(table)->width() : -1;
+}
+
+const char* macboost_table_column_name(void* table, int64_t col) {
+  if (!table) return nullptr;
+  const mb::Table& t = *static_cast<mb::Table*>(table);
+  if (col < 0 || col >= t.width()) return nullptr;
+  return t.header[size_t(t.columns[size_t(col)])].c_str();
+}
+
+const float* macboost_table_data(void* table) {
+  return table ? static_cast<mb::Table*>(table)->data : nullptr;
+}
+
+void macboost_table_free(void* table) { delete static_cast<mb::Table*>(table); }
+
+int32_t macboost_write_predictions(const float* preds, int64_t rows, int64_t k, const char* path,
+                                   char** err) {
+  std::string e;
+  if (!mb::write_predictions(preds, rows, k, path, e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_cli_predict(void* handle, const char* data_path, int32_t format, int32_t raw,
+                             const int32_t* devices, int32_t ndev, const char* output_path,
+                             int64_t* rows_out, char** err) {
+  if (!handle || !data_path || !output_path || (ndev > 0 && !devices) || ndev < 0) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::vector<int> devs(devices, devices + ndev);
+  if (devs.empty()) devs = default_devices();
+  std::string e;
+  if (!mb::cli_predict(*engine(handle), data_path, format, raw != 0, devs, output_path, rows_out,
+                       e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
 }
 
 }  // extern "C"
