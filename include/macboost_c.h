@@ -68,8 +68,22 @@ void macboost_free(void *handle);
  * Replaces CAPI.swift:305-308. */
 void macboost_free_string(char *s);
 
+/* TreeSHAP feature contributions of feature-major x into out (rows x K x
+ * (cols + 1) floats; per row and class the cols contributions then the
+ * expected value; K = macboost_num_classes).  Replaces
+ * macboost_predict_contrib, CAPI.swift:222-240 (MacBooster.predictContributions,
+ * SHAP.swift:39-52): path-dependent TreeSHAP with node covers as the
+ * background, evaluated on the GPU in float64 and rounded to float32; per
+ * class, contributions plus expected value sum to the raw margin.  Trees
+ * without covers add nothing (their expectation is not part of the bias).
+ * Fails for NULL arguments, cols != num_features, a cover array whose length
+ * is not the tree's node count, or a path through more than 32 distinct
+ * features.  Devices as macboost_predict. */
+int32_t macboost_predict_contrib(void *handle, const float *x, int64_t rows, int64_t cols,
+                                 float *out, char **err);
+
 /* Training-side entry points of the reference ABI (CAPI.swift:86-135,
- * 138-183, 223-240).  This library is an inference engine: they exist so that
+ * 138-183).  This library is an inference engine: they exist so that
  * bindings written for the full ABI load it unchanged, and they fail with a
  * message ("not supported by this inference engine"). */
 void *macboost_train(const char *params_json, const float *x, int64_t rows, int64_t cols,
@@ -79,8 +93,6 @@ int32_t macboost_select_features(const char *params_json, const float *x, int64_
                                  int64_t cols, const float *y, const float *w, int32_t rounds,
                                  int32_t trees, float alpha, int64_t seed, int32_t *out_hits,
                                  int32_t *out_decision, float *out_gain_ratio, char **err);
-int32_t macboost_predict_contrib(void *handle, const float *x, int64_t rows, int64_t cols,
-                                 float *out, char **err);
 
 /* ---- additive entry points (no counterpart in the reference ABI) -------- */
 
@@ -121,6 +133,12 @@ int32_t macboost_predict_ex(void *handle, const float *x, int64_t rows, int64_t 
 int32_t macboost_predict_device(void *handle, int32_t device, const float *x_dev, int64_t rows,
                                 int64_t cols, int64_t ld, int32_t layout, int32_t kind,
                                 void *out_dev, void *stream, char **err);
+
+/* macboost_predict_contrib with a layout (MACBOOST_LAYOUT_*) and a device
+ * list (ndev == 0: the current device); rows shard over the devices. */
+int32_t macboost_predict_contrib_ex(void *handle, const float *x, int64_t rows, int64_t cols,
+                                    int32_t layout, const int32_t *devices, int32_t ndev,
+                                    float *out, char **err);
 
 /* Upload the model to the listed devices now (otherwise done on first use). */
 int32_t macboost_prepare(void *handle, const int32_t *devices, int32_t ndev, char **err);

@@ -69,6 +69,8 @@ def _configure(lib):
         "macboost_kernel_launches": (ctypes.c_uint64, []),
         "macboost_host_alloc": (P, [I64]),
         "macboost_host_free": (None, [P]),
+        "macboost_predict_contrib": (I32, [P, _f32_p, I64, I64, _f32_p, _c_char_pp]),
+        "macboost_predict_contrib_ex": (I32, [P, P, I64, I64, I32, _i32_p, I32, P, _c_char_pp]),
         "macboost_num_feature_names": (I64, [P]),
         "macboost_feature_name": (ctypes.c_char_p, [P, I64]),
         "macboost_table_read": (P, [ctypes.c_char_p, I32, _c_char_pp]),
@@ -210,6 +212,50 @@ def predict(handle: _Handle, X) -> np.ndarray:
     if rc != 0:
         raise MacBoostError(_take_error(err))
     return out.reshape(rows, k) if k > 1 else out
+
+
+def predict_contrib(handle: _Handle, X) -> np.ndarray:
+    """The reference binding's predict_contrib (_core.py:222-231): SHAP
+    contributions, (rows, K * (cols + 1)) float32; per class the cols
+    contributions then the expected value."""
+    Xf, rows, cols = _feature_major(X)
+    k = _lib.macboost_num_classes(handle.ptr)
+    out = np.empty(rows * k * (cols + 1), dtype=np.float32)
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict_contrib(handle.ptr, _f32(Xf), rows, cols, _f32(out),
+                                       ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
+    return out.reshape(rows, k * (cols + 1))
+
+
+def predict_contrib_ex(handle: _Handle, X, layout: str = "row", devices=None) -> np.ndarray:
+    """SHAP contributions with the input layout and device list of predict_ex."""
+    a = np.asarray(X, dtype=np.float32)
+    if a.ndim != 2:
+        raise ValueError(f"X must be 2-dimensional, got shape {a.shape}")
+    a = np.ascontiguousarray(a)
+    if layout == "row":
+        rows, cols = a.shape
+        lay = LAYOUT_ROW_MAJOR
+    elif layout == "feature":
+        cols, rows = a.shape
+        lay = LAYOUT_FEATURE_MAJOR
+    else:
+        raise ValueError("layout must be 'row' or 'feature'")
+    k = _lib.macboost_num_classes(handle.ptr)
+    out = np.empty((rows, k * (cols + 1)), dtype=np.float32)
+    devs = None
+    nd = 0
+    if devices:
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        nd = len(devices)
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict_contrib_ex(handle.ptr, a.ctypes.data, rows, cols, lay, devs, nd,
+                                          out.ctypes.data, ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
+    return out
 
 
 def predict_ex(handle: _Handle, X, kind: int = KIND_PREDICT, layout: str = "row",

@@ -263,9 +263,34 @@ int32_t macboost_select_features(const char*, const float*, int64_t, int64_t, co
   return 1;
 }
 
-int32_t macboost_predict_contrib(void*, const float*, int64_t, int64_t, float*, char** err) {
-  set_error(err, std::string("SHAP contributions are ") + kNoTraining);
-  return -1;
+int32_t macboost_predict_contrib(void* handle, const float* x, int64_t rows, int64_t cols,
+                                 float* out, char** err) {
+  if (!handle || !x || !out) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::engine_contrib_host(*engine(handle), x, rows, cols, 0, default_devices(), out, e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_predict_contrib_ex(void* handle, const float* x, int64_t rows, int64_t cols,
+                                    int32_t layout, const int32_t* devices, int32_t ndev,
+                                    float* out, char** err) {
+  if (!handle || !x || !out || (ndev > 0 && !devices) || ndev < 0) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::vector<int> devs(devices, devices + ndev);
+  std::string e;
+  if (mb::engine_contrib_host(*engine(handle), x, rows, cols, layout, devs, out, e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
 }
 
 int64_t macboost_num_feature_names(void* handle) {

@@ -147,7 +147,12 @@ DeviceState::~DeviceState() {
                   static_cast<void*>(conv_src), static_cast<void*>(conv_dst),
                   static_cast<void*>(search), static_cast<void*>(bin_plan),
                   static_cast<void*>(masks), static_cast<void*>(leaf_heap),
-                  static_cast<void*>(base), static_cast<void*>(err)})
+                  static_cast<void*>(base), static_cast<void*>(err), shap_paths, shap_uniq,
+                  static_cast<void*>(shap_masks), static_cast<void*>(shap_block_path),
+                  static_cast<void*>(shap_block_uniq), static_cast<void*>(shap_class_block),
+                  static_cast<void*>(shap_coef), static_cast<void*>(shap_feature_slot),
+                  static_cast<void*>(shap_slot_feature), static_cast<void*>(shap_bias),
+                  static_cast<void*>(shap_scratch)})
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
     if (xbuf[i]) cudaFree(xbuf[i]);
@@ -228,6 +233,7 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   auto d = std::make_unique<DeviceState>();
   d->device = device;
   d->num_sms = prop.multiProcessorCount;
+  d->smem_optin = size_t(prop.sharedMemPerBlockOptin);
   std::vector<float> base = e.model.base_scores;
   std::vector<unsigned long long> boff(e.flat.block_off.begin(), e.flat.block_off.end());
   if (boff.empty()) boff.push_back(0);
@@ -284,7 +290,7 @@ int check_err_word(DeviceState& d, std::string& err) {
   if (w != 0) {
     cudaMemset(d.err, 0, sizeof(unsigned));
     err = "device " + std::to_string(d.device) +
-          ": forest kernel gave up waiting for a shared-memory transfer (status " +
+          ": a kernel gave up waiting for a shared-memory transfer (status " +
           std::to_string(w) + ")";
     return -1;
   }
@@ -530,6 +536,273 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
     return -1;
   }
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return 0;
+}
+
+}  // namespace mb
+
+// ---- TreeSHAP contributions -------------------------------------------------
+
+namespace mb {
+namespace {
+
+int upload_bytes(void*& dst, const void* src, size_t bytes, std::string& err) {
+  MB_CUDA(cudaMalloc(&dst, std::max<size_t>(bytes, 16)), "cudaMalloc (SHAP tables)");
+  if (bytes) MB_CUDA(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice), "cudaMemcpy (SHAP)");
+  return 0;
+}
+
+bool ensure_shap_built(Engine& e, std::string& err) {
+  std::lock_guard<std::mutex> lk(e.shap_mu);
+  if (e.shap_state == 0) {
+    std::string why;
+    e.shap_state = build_shap(e.model, e.shap, why) ? 1 : -1;
+    e.shap_err = why;
+  }
+  if (e.shap_state < 0) {
+    err = e.shap_err;
+    return false;
+  }
+  return true;
+}
+
+// Upload the path tables to `d` and pick the launch plan: the largest row
+// tile (128, 64 or 32 rows) that keeps the most rows resident per SM with
+// the tile and its float64 accumulators in shared memory, else 128-row
+// tiles with both in global memory.  Called with d.mu held.
+int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
+  if (d.shap_ready) return 0;
+  const ShapForest& s = e.shap;
+  const int S = int(s.slot_feature.size());
+  const int maxu = std::max(s.max_unique, 1);
+  void* p = nullptr;
+  if (upload_bytes(d.shap_paths, s.paths.data(), s.paths.size() * sizeof(ShapPathRec), err) ||
+      upload_bytes(d.shap_uniq, s.uniq.data(), s.uniq.size() * sizeof(ShapUniqueRec), err))
+    return -1;
+  if (upload_bytes(p, s.masks.data(), s.masks.size() * 4, err)) return -1;
+  d.shap_masks = static_cast<unsigned*>(p);
+  if (upload_bytes(p, s.block_path.data(), s.block_path.size() * 4, err)) return -1;
+  d.shap_block_path = static_cast<unsigned*>(p);
+  if (upload_bytes(p, s.block_uniq.data(), s.block_uniq.size() * 4, err)) return -1;
+  d.shap_block_uniq = static_cast<unsigned*>(p);
+  if (upload_bytes(p, s.class_block.data(), s.class_block.size() * 4, err)) return -1;
+  d.shap_class_block = static_cast<unsigned*>(p);
+  if (upload_bytes(p, s.coef.data(), s.coef.size() * 8, err)) return -1;
+  d.shap_coef = static_cast<double*>(p);
+  if (upload_bytes(p, s.feature_slot.data(), s.feature_slot.size() * 4, err)) return -1;
+  d.shap_feature_slot = static_cast<int*>(p);
+  if (upload_bytes(p, s.slot_feature.data(), s.slot_feature.size() * 4, err)) return -1;
+  d.shap_slot_feature = static_cast<int*>(p);
+  if (upload_bytes(p, s.bias.data(), s.bias.size() * 4, err)) return -1;
+  d.shap_bias = static_cast<float*>(p);
+  int best_rows = 0;
+  for (int R : {128, 64, 32}) {
+    const size_t smem = shap_smem_bytes(maxu, true, S, R);
+    if (smem > d.smem_optin) continue;
+    int ctas = 0;
+    MB_CUDA(shap_occupancy(maxu, true, R, smem, &ctas), "occupancy query (SHAP)");
+    if (ctas * R > best_rows) {
+      best_rows = ctas * R;
+      d.shap_R = R;
+      d.shap_smem = smem;
+      d.shap_grid = ctas * d.num_sms;
+      d.shap_in_smem = true;
+    }
+  }
+  if (best_rows == 0) {
+    const int R = 128;
+    const size_t smem = shap_smem_bytes(maxu, false, S, R);
+    int ctas = 0;
+    MB_CUDA(shap_occupancy(maxu, false, R, smem, &ctas), "occupancy query (SHAP)");
+    if (ctas < 1) {
+      err = "the contributions kernel cannot be resident on an SM";
+      return -1;
+    }
+    d.shap_R = R;
+    d.shap_smem = smem;
+    d.shap_grid = std::min(ctas, 2) * d.num_sms;  // bounds the scratch: S x 1 KiB per CTA
+    d.shap_in_smem = false;
+    MB_CUDA(cudaMalloc(reinterpret_cast<void**>(&d.shap_scratch),
+                       size_t(d.shap_grid) * size_t(S) * R * sizeof(double)),
+            "cudaMalloc (SHAP accumulators)");
+  }
+  d.shap_ready = true;
+  return 0;
+}
+
+// One GPU's share [r_begin, r_end) of a host-memory contributions call:
+// double-buffered chunks as in run_slice (H2D of the used feature columns,
+// kernel, D2H of the chunk's rows x K x (F + 1) block).
+int run_contrib_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t cols,
+                      int layout, int64_t r_begin, int64_t r_end, float* out, std::string& err) {
+  std::lock_guard<std::mutex> lk(d.mu);
+  DeviceGuard g(d.device);
+  if (prepare_shap(e, d, err)) return -1;
+  const int64_t n = r_end - r_begin;
+  if (n <= 0) return 0;
+  const ShapForest& s = e.shap;
+  const int S = int(s.slot_feature.size());
+  const int K = e.model.K;
+  const int64_t W = cols + 1;
+  const int R = d.shap_R;
+  const int64_t in_row = std::max<int64_t>(layout == 1 ? cols : S, 1) * 4;
+  const int64_t out_row = int64_t(K) * W * 4;
+  const int64_t budget = int64_t(256) << 20;
+  int64_t C = std::min(budget / in_row, budget / out_row);
+  C = std::max<int64_t>(C / R * R, R);
+  if (C > n) C = (n + 3) / 4 * 4;
+  const int64_t ldc = (C + 3) / 4 * 4;
+  for (int p = 0; p < 2; ++p) {
+    if (ensure(reinterpret_cast<void*&>(d.xbuf[p]), d.xcap[p],
+               size_t(std::max<int64_t>(layout == 1 ? cols : S, 1)) * ldc * 4, err))
+      return -1;
+    if (layout == 1 &&
+        ensure(reinterpret_cast<void*&>(d.xraw[p]), d.rcap[p], size_t(cols) * C * 4 + 16, err))
+      return -1;
+    if (ensure(d.obuf[p], d.ocap[p], size_t(out_row) * C + 16, err)) return -1;
+  }
+  // runs of slots whose features are consecutive (one 2-D copy each)
+  std::vector<std::pair<int64_t, int64_t>> runs;  // (first feature, count)
+  for (int sl = 0; sl < S; ++sl) {
+    const int64_t feat = s.slot_feature[size_t(sl)];
+    if (!runs.empty() && runs.back().first + runs.back().second == feat)
+      ++runs.back().second;
+    else
+      runs.push_back({feat, 1});
+  }
+  int64_t prev_r0 = -1, prev_n = 0;
+  int prev_p = 0;
+  auto drain = [&](int p, int64_t r0, int64_t nr) -> int {
+    MB_CUDA(cudaMemcpyAsync(out + size_t(r0) * size_t(K * W), d.obuf[p], size_t(nr) * out_row,
+                            cudaMemcpyDeviceToHost, d.stream[p]),
+            "cudaMemcpyAsync (contributions)");
+    return 0;
+  };
+  int c = 0;
+  for (int64_t r0 = r_begin; r0 < r_end; r0 += C, ++c) {
+    const int p = c & 1;
+    const int64_t nr = std::min(C, r_end - r0);
+    cudaStream_t st = d.stream[p];
+    const int* slot_map = nullptr;
+    if (layout == 0) {
+      int64_t slot = 0;
+      for (auto& run : runs) {
+        MB_CUDA(cudaMemcpy2DAsync(d.xbuf[p] + slot * ldc, size_t(ldc) * 4,
+                                  x + run.first * rows + r0, size_t(rows) * 4, size_t(nr) * 4,
+                                  size_t(run.second), cudaMemcpyHostToDevice, st),
+                "cudaMemcpy2DAsync (features)");
+        slot += run.second;
+      }
+    } else {
+      MB_CUDA(cudaMemcpyAsync(d.xraw[p], x + r0 * cols, size_t(nr) * cols * 4,
+                              cudaMemcpyHostToDevice, st),
+              "cudaMemcpyAsync (rows)");
+      MB_CUDA(launch_transpose(d.xraw[p], nr, int(cols), d.xbuf[p], ldc, st), "transpose launch");
+      slot_map = d.shap_slot_feature;
+    }
+    ShapArgs a{};
+    a.x = d.xbuf[p];
+    a.rows = nr;
+    a.ld = ldc;
+    a.slot_map = slot_map;
+    a.S = S;
+    a.paths = d.shap_paths;
+    a.uniq = d.shap_uniq;
+    a.masks = d.shap_masks;
+    a.block_path = d.shap_block_path;
+    a.block_uniq = d.shap_block_uniq;
+    a.class_block = d.shap_class_block;
+    a.err = d.err;
+    a.coef = d.shap_coef;
+    a.feature_slot = d.shap_feature_slot;
+    a.bias = d.shap_bias;
+    a.K = K;
+    a.F = int(cols);
+    a.data_bins = e.model.num_bins - 1;
+    a.out = static_cast<float*>(d.obuf[p]);
+    a.scratch = d.shap_scratch;
+    a.R = R;
+    a.ntiles = (nr + R - 1) / R;
+    const int grid = int(std::min<int64_t>(d.shap_grid, a.ntiles));
+    MB_CUDA(launch_shap(a, std::max(s.max_unique, 1), d.shap_in_smem, d.shap_smem, grid, st),
+            "contributions kernel launch");
+    g_kernel_launches.fetch_add(1);
+    if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
+    prev_r0 = r0;
+    prev_n = nr;
+    prev_p = p;
+  }
+  if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
+  MB_CUDA(cudaStreamSynchronize(d.stream[0]), "contributions (stream 0)");
+  MB_CUDA(cudaStreamSynchronize(d.stream[1]), "contributions (stream 1)");
+  return check_err_word(d, err);
+}
+
+}  // namespace
+
+int engine_contrib_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
+                        const std::vector<int>& devices_in, float* out, std::string& err) {
+  if (rows < 0) {
+    err = "rows must be >= 0";
+    return -1;
+  }
+  if (cols != e.model.num_features) {
+    err = "model expects " + std::to_string(e.model.num_features) + " features, got " +
+          std::to_string(cols);
+    return -1;
+  }
+  if (layout != 0 && layout != 1) {
+    err = "layout must be 0 (feature-major) or 1 (row-major)";
+    return -1;
+  }
+  if (!ensure_shap_built(e, err)) return -1;
+  if (rows == 0) return 0;
+  if (!x || !out) {
+    err = "null argument";
+    return -1;
+  }
+  std::vector<int> devices = devices_in;
+  if (devices.empty()) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    devices.push_back(cur);
+  }
+  std::vector<DeviceState*> ds;
+  for (int dev : devices) {
+    DeviceState* d = engine_prepare(e, dev, err);
+    if (!d) return -1;
+    if (std::find(ds.begin(), ds.end(), d) != ds.end()) {
+      err = "device " + std::to_string(dev) + " listed twice";
+      return -1;
+    }
+    ds.push_back(d);
+  }
+  const int nd = int(ds.size());
+  std::vector<std::string> errs(static_cast<size_t>(nd));
+  std::vector<int> rcs(static_cast<size_t>(nd), 0);
+  std::vector<std::thread> th;
+  for (int gi = 0; gi < nd; ++gi) {
+    const int64_t a = rows * gi / nd, b = rows * (gi + 1) / nd;
+    auto job = [&, gi, a, b] {
+      rcs[size_t(gi)] =
+          run_contrib_slice(e, *ds[size_t(gi)], x, rows, cols, layout, a, b, out, errs[size_t(gi)]);
+    };
+    if (nd == 1) {
+      job();
+      break;
+    }
+    try {
+      th.emplace_back(job);
+    } catch (...) {
+      job();
+    }
+  }
+  for (auto& t : th) t.join();
+  for (int gi = 0; gi < nd; ++gi)
+    if (rcs[size_t(gi)] != 0) {
+      err = errs[size_t(gi)];
+      return -1;
+    }
   return 0;
 }
 

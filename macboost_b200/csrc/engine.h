@@ -14,6 +14,7 @@
 #include "forest.h"
 #include "kernels.h"
 #include "model.h"
+#include "shap.h"
 
 namespace mb {
 
@@ -43,6 +44,24 @@ struct DeviceState {
   size_t rcap[2] = {0, 0};
   void* obuf[2] = {nullptr, nullptr};
   size_t ocap[2] = {0, 0};
+  size_t smem_optin = 0;                // shared memory a block may opt in to
+  // TreeSHAP tables, uploaded on the first contributions call
+  bool shap_ready = false;
+  void* shap_paths = nullptr;
+  void* shap_uniq = nullptr;
+  unsigned* shap_masks = nullptr;
+  unsigned* shap_block_path = nullptr;
+  unsigned* shap_block_uniq = nullptr;
+  unsigned* shap_class_block = nullptr;
+  double* shap_coef = nullptr;
+  int* shap_feature_slot = nullptr;
+  int* shap_slot_feature = nullptr;
+  float* shap_bias = nullptr;
+  double* shap_scratch = nullptr;       // accumulators when they do not fit in shared memory
+  int shap_R = 0;
+  bool shap_in_smem = true;
+  size_t shap_smem = 0;
+  int shap_grid = 0;
   std::mutex mu;                        // one predict at a time per (model, device)
   ~DeviceState();
 };
@@ -53,6 +72,11 @@ struct Engine {
   std::string description;
   std::mutex mu;                        // guards `devices`
   std::map<int, std::unique_ptr<DeviceState>> devices;
+  // TreeSHAP path tables, built on the first contributions call
+  std::mutex shap_mu;
+  int shap_state = 0;                   // 0 not built, 1 built, -1 failed (shap_err)
+  std::string shap_err;
+  ShapForest shap;
 };
 
 // Global count of forest-kernel launches (for benchmarking claims).
@@ -75,6 +99,11 @@ int engine_predict_host(Engine& e, const float* x, int64_t rows, int64_t cols, i
 int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, int64_t cols,
                           int64_t ld, int layout, int kind, void* out, cudaStream_t stream,
                           std::string& err);
+
+// TreeSHAP contributions from host memory (rows x K x (cols + 1) float32),
+// rows sharded over `devices` like engine_predict_host.
+int engine_contrib_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
+                        const std::vector<int>& devices, float* out, std::string& err);
 
 // Synchronise `device` and report any kernel-side error since the last check.
 int engine_check_device(Engine& e, int device, std::string& err);

@@ -70,6 +70,36 @@ cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, siz
 cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
                              size_t smem, int* ctas, int code_bytes = 1);
 
+// TreeSHAP contributions (kernels_shap.cu).  Rows: feature-major
+// x[slot_map[s] * ld + i] (x[s * ld + i] when slot_map is null) for the S
+// staged slots; output rows x K x (F + 1) float32.
+struct ShapArgs {
+  const float* x;
+  long long rows, ld;
+  const int* slot_map;
+  int S;
+  const void* paths;            // ShapPathRec[...]
+  const void* uniq;             // ShapUniqueRec[...]
+  const unsigned* masks;        // admitted-code sets, 8 words each
+  const unsigned* block_path;   // [nblocks + 1] path boundaries of the staged blocks
+  const unsigned* block_uniq;   // [nblocks + 1] unique-record boundaries
+  const unsigned* class_block;  // [K + 1] block boundaries per class
+  const double* coef;           // Shapley weights, (kShapMaxUnique + 1) x kShapCoefRow
+  const int* feature_slot;      // [F]
+  const float* bias;            // [K]
+  int K, F, data_bins;
+  float* out;
+  double* scratch;              // global accumulators (gridDim x S x R) when not in shared memory
+  int R;                        // rows per CTA (= threads per CTA, <= 128)
+  long long ntiles;
+  unsigned* err;                // kErrWaitTimeout when a staged block never arrived
+};
+// Dynamic shared memory of the contributions kernel (maxu: longest path in
+// distinct features; smem_variant: row tile and accumulators in shared memory).
+size_t shap_smem_bytes(int maxu, bool smem_variant, int S, int R);
+cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas);
+cudaError_t launch_shap(const ShapArgs& a, int maxu, bool smem_variant, size_t smem, int grid,
+                        cudaStream_t stream);
 // Row-major [rows][F] -> feature-major [F][ld] (ld >= rows).
 cudaError_t launch_transpose(const float* in, long long rows, int F, float* out, long long ld,
                              cudaStream_t stream);

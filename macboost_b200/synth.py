@@ -271,6 +271,47 @@ def make_model(cfg: Config | str, trees: int | None = None, seed: int | None = N
     return model
 
 
+def add_covers(model: dict, X: np.ndarray) -> dict:
+    """Give every tree a `cover` array: the number of rows of X (row-major,
+    numFeatures columns) that reach each node, which is what a trainer with
+    unit hessians stores (Booster.swift:126).  Routing as the predictor:
+    categorical mask bit, NaN to the default side, else v <= threshold."""
+    X = np.asarray(X, dtype=np.float32)
+    data_bins = int(model["numBins"]) - 1
+    for t in model["trees"]:
+        feat = np.asarray(t["feature"], dtype=np.int64)
+        thr = np.asarray(t["threshold"], dtype=np.float32)
+        flags = np.asarray(t["flags"], dtype=np.int64)
+        mask = t.get("catMask")
+        mask = None if mask is None or len(mask) == 0 else np.asarray(mask, dtype=np.uint64)
+        cover = np.zeros(len(feat), dtype=np.float64)
+        idx = np.arange(len(X))
+        node = np.zeros(len(X), dtype=np.int64)
+        while idx.size:
+            np.add.at(cover, node, 1.0)
+            f = feat[node]
+            inner = f >= 0
+            idx, node, f = idx[inner], node[inner], f[inner]
+            if not idx.size:
+                break
+            v = X[idx, f]
+            fl = flags[node]
+            with np.errstate(invalid="ignore"):
+                left = np.where(np.isnan(v), (fl & 1) != 0, v <= thr[node])
+                if mask is not None:
+                    cat = (fl & 2) != 0
+                    if cat.any():
+                        vc = v[cat]
+                        r = np.rint(vc)
+                        ok = np.isfinite(vc) & (r >= 0) & (r < data_bins)
+                        code = np.where(ok, r, data_bins).astype(np.int64)
+                        w = mask[node[cat] * 8 + code // 32]
+                        left[cat] = ((w >> (code % 32).astype(np.uint64)) & 1) == 1
+            node = 2 * node + 1 + (~left).astype(np.int64)
+        t["cover"] = cover.astype(np.float32)
+    return model
+
+
 def _fmt_list(a: np.ndarray) -> str:
     # float32 values are written as the exact repr of their float64 value, so
     # any reader that parses to float64 and rounds to float32 recovers them.
@@ -292,12 +333,14 @@ def model_to_json(model: dict) -> str:
         if i:
             parts.append(",")
         mask = t.get("catMask")
-        parts.append('{"feature":%s,"threshold":%s,"leaf":%s,"flags":%s,"catMask":%s}' % (
+        cover = t.get("cover")
+        parts.append('{"feature":%s,"threshold":%s,"leaf":%s,"flags":%s,"catMask":%s%s}' % (
             _fmt_list(np.asarray(t["feature"], dtype=np.int32)),
             _fmt_list(np.asarray(t["threshold"], dtype=np.float32)),
             _fmt_list(np.asarray(t["leaf"], dtype=np.float32)),
             _fmt_list(np.asarray(t["flags"], dtype=np.uint8)),
-            "[]" if mask is None or len(mask) == 0 else _fmt_list(np.asarray(mask, np.uint32))))
+            "[]" if mask is None or len(mask) == 0 else _fmt_list(np.asarray(mask, np.uint32)),
+            "" if cover is None else ',"cover":' + _fmt_list(np.asarray(cover, np.float32))))
     parts.append("]")
     if model.get("numClasses") is not None:
         parts.append(',"numClasses":%d' % model["numClasses"])

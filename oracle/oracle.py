@@ -34,13 +34,15 @@ LOG_LINK_OBJECTIVES = (5, 6)   # poisson, tweedie (Booster.swift:15)
 
 
 def build(force: bool = False) -> Path:
-    """Compile mbref.c into oracle/libmbref.so with gcc (no fast-math)."""
-    src = HERE / "mbref.c"
-    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    """Compile mbref.c and mbshap.c into oracle/libmbref.so with gcc (no
+    fast-math, no contraction of multiply-adds)."""
+    srcs = [HERE / "mbref.c", HERE / "mbshap.c"]
+    if force or not LIB_PATH.exists() or any(LIB_PATH.stat().st_mtime < s.stat().st_mtime
+                                             for s in srcs):
         import subprocess
         tmp = LIB_PATH.with_suffix(f".so.tmp{os.getpid()}")
         subprocess.run(["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-ffp-contract=off",
-                        "-fno-fast-math", "-pthread", "-o", str(tmp), str(src), "-lm"],
+                        "-fno-fast-math", "-pthread", "-o", str(tmp), *map(str, srcs), "-lm"],
                        check=True)
         os.replace(tmp, LIB_PATH)
     return LIB_PATH
@@ -60,6 +62,10 @@ def _load():
         lib.mbref_predict.argtypes = [P, ctypes.c_int32, P, P, P, P, P, P, ctypes.c_int32,
                                       ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int64, ctypes.c_int32, P, P, ctypes.c_int32]
+        lib.mbref_shap.restype = ctypes.c_int32
+        lib.mbref_shap.argtypes = [P, ctypes.c_int32, P, P, P, P, P, P, P, P, ctypes.c_int32,
+                                   ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64,
+                                   ctypes.c_int64, ctypes.c_int32, P, ctypes.c_int32]
         _lib = lib
     return _lib
 
@@ -78,6 +84,8 @@ class OracleModel:
     flags: np.ndarray            # uint8[N]
     catmask: np.ndarray          # uint32[N*8]
     has_mask: np.ndarray         # uint8[T]
+    cover: np.ndarray | None = None      # float32[N] (0 where a tree has none)
+    has_cover: np.ndarray | None = None  # uint8[T]
 
     @property
     def num_trees(self) -> int:
@@ -97,11 +105,17 @@ def model_from_dict(m: dict) -> OracleModel:
     K = int(m.get("numClasses") or 1)
     base = np.asarray(m.get("baseScores") or [m["baseScore"]], dtype=np.float32)
     feats, thrs, leaves, flags, masks, has = [], [], [], [], [], []
+    covers, has_cov = [], []
     off = [0]
     for t in m["trees"]:
         f = np.asarray(t["feature"], dtype=np.int64).astype(np.int32)
         n = len(f)
         feats.append(f)
+        cv = np.asarray(t.get("cover") or [], dtype=np.float32)
+        if cv.size not in (0, n):
+            raise ValueError(f"a tree has {cv.size} cover values for {n} nodes")
+        covers.append(cv if cv.size else np.zeros(n, np.float32))
+        has_cov.append(1 if cv.size else 0)
         thrs.append(np.asarray(t["threshold"], dtype=np.float32))
         leaves.append(np.asarray(t["leaf"], dtype=np.float32))
         flags.append(np.asarray(t["flags"], dtype=np.uint8))
@@ -123,7 +137,8 @@ def model_from_dict(m: dict) -> OracleModel:
         tree_off=np.asarray(off, dtype=np.int64), feature=cat(feats, np.int32),
         threshold=cat(thrs, np.float32), leaf=cat(leaves, np.float32),
         flags=cat(flags, np.uint8), catmask=cat(masks, np.uint32),
-        has_mask=np.asarray(has, dtype=np.uint8))
+        has_mask=np.asarray(has, dtype=np.uint8), cover=cat(covers, np.float32),
+        has_cover=np.asarray(has_cov, dtype=np.uint8))
 
 
 def _ptr(a):
@@ -158,6 +173,96 @@ def predict_raw(model: OracleModel, X, layout: str = "row", want_leaf: bool = Fa
     if rc != 0:
         raise RuntimeError("mbref_predict rejected its arguments")
     return (out, leaf) if want_leaf else out
+
+
+def predict_contrib(model: OracleModel, X, layout: str = "row", nthreads: int | None = None):
+    """TreeSHAP contributions, float32 (rows, K * (F + 1)): per class the F
+    feature contributions then the expected value (mbshap.c restating
+    Sources/MacBoost/SHAP.swift:170-326 and :56-72)."""
+    lib = _load()
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    if layout == "row":
+        rows, cols = X.shape
+        lay, ld = 1, cols
+    else:
+        cols, rows = X.shape
+        lay, ld = 0, rows
+    if cols != model.num_features:
+        raise ValueError(f"model expects {model.num_features} features, got {cols}")
+    K, T = model.num_classes, model.num_trees
+    out = np.empty((rows, K * (cols + 1)), dtype=np.float32)
+    rc = lib.mbref_shap(
+        _ptr(model.tree_off), T, _ptr(model.feature), _ptr(model.threshold), _ptr(model.leaf),
+        _ptr(model.flags), _ptr(model.catmask), _ptr(model.has_mask), _ptr(model.cover),
+        _ptr(model.has_cover), model.num_bins - 1, K, _ptr(model.base_scores), _ptr(X), rows,
+        cols, ld, lay, out.ctypes.data if out.size else None, nthreads or os.cpu_count() or 1)
+    if rc != 0:
+        raise RuntimeError("mbref_shap rejected its arguments")
+    return out
+
+
+def shapley_bruteforce(model: OracleModel, x: np.ndarray) -> np.ndarray:
+    """Exact Shapley values of one row from their definition, as an
+    independent check of the TreeSHAP restatement: the value of a coalition S
+    is the tree's expectation with the features outside S integrated out by
+    node cover fractions (Lundberg et al. 2020, Algorithm 1; a node with zero
+    cover gives its children fraction 0, as the reference does), and
+    phi_j = sum over S not containing j of |S|!(M-|S|-1)!/M! (v(S+j) - v(S)).
+    Pure Python, exponential in the number of features: tiny models only.
+    Returns float64 (K, F + 1), the last column the expected value v({})."""
+    from itertools import combinations
+    from math import factorial
+
+    F, K = model.num_features, model.num_classes
+    x = np.asarray(x, dtype=np.float32)
+
+    def goes_left(t, g, v):
+        fl = int(model.flags[g])
+        if (fl & 2) and model.has_mask[t]:
+            c = model.num_bins - 1
+            if np.isfinite(v):
+                r = np.rint(v)
+                if 0 <= r < model.num_bins - 1:
+                    c = int(r)
+            return (int(model.catmask[g * 8 + c // 32]) >> (c % 32)) & 1 == 1
+        if np.isnan(v):
+            return (fl & 1) != 0
+        return bool(v <= model.threshold[g])
+
+    def expect(t, n, S):
+        b = int(model.tree_off[t])
+        f = int(model.feature[b + n])
+        if f < 0:
+            return float(model.leaf[b + n])
+        left, right = 2 * n + 1, 2 * n + 2
+        if f in S:
+            return expect(t, left if goes_left(t, b + n, x[f]) else right, S)
+        cn = float(model.cover[b + n])
+        # cover fractions, 0 below a node no training row reached (SHAP.swift:241-242)
+        fl = float(model.cover[b + left]) / cn if cn > 0 else 0.0
+        fr = float(model.cover[b + right]) / cn if cn > 0 else 0.0
+        return fl * expect(t, left, S) + fr * expect(t, right, S)
+
+    out = np.zeros((K, F + 1))
+    for k in range(K):
+        out[k, F] = float(model.base_scores[k])
+    for t in range(model.num_trees):
+        if not model.has_cover[t] or not model.cover[model.tree_off[t]] > 0:
+            continue
+        k = t % K
+        v = {}
+        for r in range(F + 1):
+            for S in combinations(range(F), r):
+                v[S] = expect(t, 0, set(S))
+        out[k, F] += v[()]
+        for j in range(F):
+            others = [i for i in range(F) if i != j]
+            for r in range(F):
+                w = factorial(r) * factorial(F - r - 1) / factorial(F)
+                for S in combinations(others, r):
+                    Sj = tuple(sorted(S + (j,)))
+                    out[k, j] += w * (v[Sj] - v[S])
+    return out
 
 
 def predict(model: OracleModel, raw: np.ndarray) -> np.ndarray:
