@@ -74,6 +74,80 @@ __device__ __forceinline__ void issue_paths(const ShapArgs& a, unsigned b, uint3
   dev::bulk_g2s(dst + kStagePathBytes, static_cast<const ShapUniqueRec*>(a.uniq) + u0, ub, bar);
 }
 
+// Row-side inputs of one path evaluation.
+struct PathCtx {
+  const ShapArgs* a;
+  const double* coef_row;  // c_U(s) for this U, indexable by s in [-U, U]
+  double* phi;             // this row's accumulators: slot s at phi[s * R]
+  long long row;
+  int R;
+};
+
+// One row, one path of exactly U distinct features: straight-line code, so
+// the U deflation chains interleave.
+template <int U>
+__device__ __forceinline__ void path_fixed(const PathCtx& c, const ShapUniqueRec* uq, double v) {
+  const ShapArgs& a = *c.a;
+  float xs[U];
+  double zr[U];
+  unsigned slots[U];
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    slots[j] = uq[j].slot;
+    zr[j] = uq[j].z;
+    xs[j] = __ldg(a.x + (a.slot_map ? __ldg(a.slot_map + slots[j]) : int(slots[j])) * a.ld + c.row);
+  }
+  double E[U + 1];
+  E[0] = 1.0;
+#pragma unroll
+  for (int i = 1; i <= U; ++i) E[i] = 0.0;
+  double poff = 1.0;
+  unsigned on = 0;
+  int m = 0;
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    const float xv = xs[j];
+    const unsigned fl = uq[j].flags;
+    bool pass = isnan(xv) ? (fl & kShapNanOk) != 0 : (!(xv <= uq[j].lo) && xv <= uq[j].hi);
+    if (fl & kShapHasCat) {
+      const int cc = shap_cat_code(xv, a.data_bins);
+      pass = pass && ((__ldg(a.masks + size_t(uq[j].mask) * 8 + (cc >> 5)) >> (cc & 31)) & 1u);
+    }
+    const double zo = pass ? zr[j] : 0.0;
+    poff *= pass ? 1.0 : zr[j];
+    on |= unsigned(pass) << j;
+    m += int(pass);
+#pragma unroll
+    for (int s = j + 1; s >= 1; --s) E[s] = fma(zo, E[s - 1], E[s]);
+  }
+  double w[U + 1];  // w[i] = c_U(m - i)
+#pragma unroll
+  for (int i = 0; i <= U; ++i) w[i] = c.coef_row[m - i];
+  double goff = 0.0;
+#pragma unroll
+  for (int i = 0; i <= U; ++i) goff = fma(E[i], w[i], goff);
+  double ep[U], g[U];
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    ep[j] = 1.0;
+    g[j] = w[1 < U + 1 ? 1 : 0];
+  }
+#pragma unroll
+  for (int i = 1; i < U; ++i)
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      ep[j] = fma(-zr[j], ep[j], E[i]);
+      g[j] = fma(ep[j], w[i + 1], g[j]);
+    }
+  const double off_c = -v * goff * poff;
+  const double on_scale = v * poff;
+#pragma unroll
+  for (int j = 0; j < U; ++j) {
+    const double cj = ((on >> j) & 1u) ? on_scale * (1.0 - zr[j]) * g[j] : off_c;
+    c.phi[size_t(slots[j]) * c.R] += cj;
+  }
+}
+
 template <int MAXU, bool SMEM>
 __global__ void __launch_bounds__(128) shap_kernel(const ShapArgs a) {
   using L = ShapLayout<MAXU>;
@@ -125,7 +199,38 @@ __global__ void __launch_bounds__(128) shap_kernel(const ShapArgs a) {
           const ShapUniqueRec* uq = su + (sp[lp].first - u0);
           const int U = int(sp[lp].U);
           const double v = sp[lp].leaf;
-          const double* cU = coef + U * L::kRow + MAXU;
+          if (MAXU == 12) {
+            const PathCtx pc{&a, coef + U * L::kRow + MAXU, phi + tid, row, R};
+            switch (U) {
+              case 1: path_fixed<1>(pc, uq, v); break;
+              case 2: path_fixed<2>(pc, uq, v); break;
+              case 3: path_fixed<3>(pc, uq, v); break;
+              case 4: path_fixed<4>(pc, uq, v); break;
+              case 5: path_fixed<5>(pc, uq, v); break;
+              case 6: path_fixed<6>(pc, uq, v); break;
+              case 7: path_fixed<7>(pc, uq, v); break;
+              case 8: path_fixed<8>(pc, uq, v); break;
+              case 9: path_fixed<9>(pc, uq, v); break;
+              case 10: path_fixed<10>(pc, uq, v); break;
+              case 11: path_fixed<11>(pc, uq, v); break;
+              default: path_fixed<12>(pc, uq, v); break;
+            }
+            continue;
+          }
+          // longer paths: the same arithmetic over a run-time U
+          // the path's records and row values into registers (independent loads)
+          float xs[MAXU];
+          double zr[MAXU];
+          unsigned slots[MAXU];
+#pragma unroll
+          for (int j = 0; j < MAXU; ++j) {
+            if (j < U) {
+              slots[j] = uq[j].slot;
+              zr[j] = uq[j].z;
+              xs[j] = __ldg(a.x + (a.slot_map ? __ldg(a.slot_map + slots[j]) : int(slots[j])) * a.ld +
+                            row);
+            }
+          }
           double E[MAXU + 1];
           E[0] = 1.0;
 #pragma unroll
@@ -136,31 +241,33 @@ __global__ void __launch_bounds__(128) shap_kernel(const ShapArgs a) {
 #pragma unroll
           for (int j = 0; j < MAXU; ++j) {
             if (j >= U) break;
-            const unsigned slot = uq[j].slot;
-            const float xv =
-                __ldg(a.x + (a.slot_map ? __ldg(a.slot_map + slot) : int(slot)) * a.ld + row);
+            const float xv = xs[j];
             const unsigned fl = uq[j].flags;
             bool pass = isnan(xv) ? (fl & kShapNanOk) != 0 : (!(xv <= uq[j].lo) && xv <= uq[j].hi);
             if (fl & kShapHasCat) {
               const int c = shap_cat_code(xv, a.data_bins);
               pass = pass && ((__ldg(a.masks + size_t(uq[j].mask) * 8 + (c >> 5)) >> (c & 31)) & 1u);
             }
-            const double z = uq[j].z;
-            if (pass) {
-              on |= 1u << j;
-              ++m;
-              // E(t) <- E(t) * (1 + z t); at most j + 1 factors so far
+            // E(t) <- E(t) * (1 + z t) when the row passes (at most j + 1
+            // factors so far), else P_off <- P_off * z
+            const double zo = pass ? zr[j] : 0.0;
+            poff *= pass ? 1.0 : zr[j];
+            on |= unsigned(pass) << j;
+            m += int(pass);
 #pragma unroll
-              for (int s = j + 1; s >= 1; --s) E[s] = fma(z, E[s - 1], E[s]);
-            } else {
-              poff *= z;
-            }
+            for (int s = j + 1; s >= 1; --s) E[s] = fma(zo, E[s - 1], E[s]);
           }
+          // weights w[i] = c_U(m - i), i = 0..U (zero outside 0 <= m - i < U)
+          const double* cU = coef + U * L::kRow + MAXU + m;
+          double w[MAXU + 1];
+#pragma unroll
+          for (int i = 0; i <= MAXU; ++i)
+            if (i <= U) w[i] = cU[-i];
           double goff = 0.0;
 #pragma unroll
           for (int i = 0; i <= MAXU; ++i) {
             if (i > U) break;
-            goff = fma(E[i], cU[m - i], goff);
+            goff = fma(E[i], w[i], goff);
           }
           const double off_c = -v * goff * poff;
           const double on_scale = v * poff;
@@ -169,19 +276,19 @@ __global__ void __launch_bounds__(128) shap_kernel(const ShapArgs a) {
             if (j >= U) break;
             double c = off_c;
             if ((on >> j) & 1u) {
-              // E(t) / (1 + z_j t), term by term, dotted with the weights
-              const double z = uq[j].z;
+              // E(t) / (1 + z_j t), term by term, dotted with c_U(m - 1 - i)
+              const double z = zr[j];
               double ep = 1.0;
-              double g = cU[m - 1];
+              double g = w[1];
 #pragma unroll
               for (int i = 1; i < MAXU; ++i) {
                 if (i >= U) break;
                 ep = fma(-z, ep, E[i]);
-                g = fma(ep, cU[m - 1 - i], g);
+                g = fma(ep, w[i + 1], g);
               }
               c = on_scale * (1.0 - z) * g;
             }
-            phi[size_t(uq[j].slot) * R + tid] += c;
+            phi[size_t(slots[j]) * R + tid] += c;
           }
         }
       }
