@@ -240,6 +240,84 @@ int32_t macboost_cli_predict(void *handle, const char *data_path, int32_t format
                              const int32_t *devices, int32_t ndev, const char *output_path,
                              int64_t *rows_out, char **err);
 
+/* ---- binned data: the trainer's side of the path (additive) ------------ */
+
+/* Bin raw values into the trainer's tiled layout on `device`.  Replaces the
+ * bin_data kernel, Sources/MacBoost/Shaders.swift:41-76.  Layout of `bins`
+ * (bin_index, Shaders.swift:37-39): ceil(cols / 8) tiles of 8 features; bin
+ * (f, i) at (f / 8) * rows * 8 + i * 8 + f % 8; padding features are 0.  A
+ * NaN goes to the missing bin num_bins - 1; a categorical feature
+ * (categorical[f] == 1; NULL: none) to clamp(rint(v), 0, num_bins - 2); a
+ * numeric one to the first of its num_bins - 2 upper edges (edges[f *
+ * (num_bins - 2) + k], ascending) that is >= v, or num_bins - 2.  x is
+ * feature-major x[f * rows + i] (layout 0) or row-major (layout 1), host
+ * memory. */
+int32_t macboost_bin_data(const float *x, int64_t rows, int64_t cols, int32_t layout,
+                          const float *edges, int32_t num_bins, const uint8_t *categorical,
+                          int32_t device, uint8_t *bins, char **err);
+
+/* Walk trees in the trainer's split form over binned rows.  Replaces
+ * predict_tree_binned and assign_leaves, Shaders.swift:1741-1781, for
+ * num_trees trees at once (one call per finished tree reproduces the
+ * reference's per-iteration use).  Tree t owns nodes tree_offsets[t] ..
+ * tree_offsets[t + 1] - 1 (implicit heap, children 2n+1 / 2n+2); per node
+ * split_feature (< 0: leaf), split_bin, split_flags (bit0 missing goes left,
+ * bit1 categorical) and 8 cat_mask words; leaf_values per node.  A row goes
+ * left when its bin is set in the mask (categorical), else when it is the
+ * missing bin and bit0 is set, else when bin <= split_bin; at most max_depth
+ * splits are taken.  preds (class-major, num_classes x rows, NULL: none) gets
+ * preds[(t % num_classes) * rows + i] += leaf, tree after tree, in float32;
+ * leaf_idx (tree-major, num_trees x rows, NULL: none) the final heap index.
+ * Host memory, on `device`.  A split that names a feature >= cols or a child
+ * outside its tree fails the call. */
+int32_t macboost_predict_tree_binned(const uint8_t *bins, int64_t rows, int64_t cols,
+                                     int32_t num_bins, int32_t num_trees,
+                                     const int64_t *tree_offsets, const int32_t *split_feature,
+                                     const uint32_t *split_bin, const uint32_t *split_flags,
+                                     const uint32_t *cat_mask, const float *leaf_values,
+                                     int32_t max_depth, int32_t num_classes, int32_t device,
+                                     float *preds, int32_t *leaf_idx, char **err);
+
+/* The same with every array in device memory, enqueued on `stream` (a
+ * cudaStream_t; NULL = legacy default stream) without waiting: the form a
+ * GPU training loop calls once per tree.  A bad split ORs 2 into the
+ * device word *status instead of failing the call. */
+int32_t macboost_predict_tree_binned_device(
+    const uint8_t *bins, int64_t rows, int64_t cols, int32_t num_bins, int32_t num_trees,
+    const int64_t *tree_offsets, const int32_t *split_feature, const uint32_t *split_bin,
+    const uint32_t *split_flags, const uint32_t *cat_mask, const float *leaf_values,
+    int32_t max_depth, int32_t num_classes, int32_t device, float *preds, int32_t *leaf_idx,
+    uint32_t *status, void *stream, char **err);
+
+/* Load a MacBoost binned dataset (.mbds).  Replaces BinnedDataset.load,
+ * Sources/MacBoost/Dataset.swift:41-83 (little-endian "MBDS", version 1,
+ * tile width 8; the same "Invalid input: ..." messages).  Returns a handle
+ * (macboost_dataset_free) or NULL.  Getters return -1 / NULL for a NULL
+ * handle; arrays are owned by the handle. */
+void *macboost_dataset_load(const char *path, char **err);
+int64_t macboost_dataset_rows(void *dataset);
+int64_t macboost_dataset_cols(void *dataset);
+int32_t macboost_dataset_num_bins(void *dataset);
+const uint8_t *macboost_dataset_bins(void *dataset);  /* tiled, as macboost_bin_data */
+const float *macboost_dataset_edges(void *dataset);   /* cols x (num_bins - 2) */
+const float *macboost_dataset_labels(void *dataset);  /* rows */
+int64_t macboost_dataset_num_categorical(void *dataset);
+int64_t macboost_dataset_categorical(void *dataset, int64_t i);
+int64_t macboost_dataset_num_feature_names(void *dataset); /* -1 when the file has none */
+const char *macboost_dataset_feature_name(void *dataset, int64_t i);
+void macboost_dataset_free(void *dataset);
+
+/* A model's output of `kind` (MACBOOST_KIND_*) on every row of a binned
+ * dataset, rows sharded over devices[0..ndev) (ndev == 0: MACBOOST_DEVICES,
+ * else the current device); `out` as macboost_predict_ex.  Each numeric
+ * threshold is mapped to the bin edge it was trained at (the trainer writes
+ * threshold = edges[f * (numBins - 2) + bin], Booster.swift:938), so rows
+ * route exactly as macboost_predict_ex routes the values they were binned
+ * from (categorical ids inside 0..numBins-2).  Fails when a threshold is no
+ * edge of the dataset or the model's numFeatures / numBins differ. */
+int32_t macboost_predict_dataset(void *handle, void *dataset, int32_t kind,
+                                 const int32_t *devices, int32_t ndev, void *out, char **err);
+
 #ifdef __cplusplus
 }
 #endif

@@ -71,6 +71,22 @@ def _configure(lib):
         "macboost_host_free": (None, [P]),
         "macboost_predict_contrib": (I32, [P, _f32_p, I64, I64, _f32_p, _c_char_pp]),
         "macboost_predict_contrib_ex": (I32, [P, P, I64, I64, I32, _i32_p, I32, P, _c_char_pp]),
+        "macboost_bin_data": (I32, [P, I64, I64, I32, P, I32, P, I32, P, _c_char_pp]),
+        "macboost_predict_tree_binned": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P, I32,
+                                               I32, I32, P, P, _c_char_pp]),
+        "macboost_dataset_load": (P, [ctypes.c_char_p, _c_char_pp]),
+        "macboost_dataset_rows": (I64, [P]),
+        "macboost_dataset_cols": (I64, [P]),
+        "macboost_dataset_num_bins": (I32, [P]),
+        "macboost_dataset_bins": (P, [P]),
+        "macboost_dataset_edges": (P, [P]),
+        "macboost_dataset_labels": (P, [P]),
+        "macboost_dataset_num_categorical": (I64, [P]),
+        "macboost_dataset_categorical": (I64, [P, I64]),
+        "macboost_dataset_num_feature_names": (I64, [P]),
+        "macboost_dataset_feature_name": (ctypes.c_char_p, [P, I64]),
+        "macboost_dataset_free": (None, [P]),
+        "macboost_predict_dataset": (I32, [P, P, I32, _i32_p, I32, P, _c_char_pp]),
         "macboost_num_feature_names": (I64, [P]),
         "macboost_feature_name": (ctypes.c_char_p, [P, I64]),
         "macboost_table_read": (P, [ctypes.c_char_p, I32, _c_char_pp]),
@@ -414,3 +430,124 @@ def cli_predict(handle: _Handle, data_path, output_path, fmt: str = "csv", raw: 
                                  ctypes.byref(rows), ctypes.byref(err)) != 0:
         raise MacBoostError(_take_error(err))
     return rows.value
+
+
+# ---- binned data (the trainer's tiled bin layout) -------------------------
+
+def bin_data(X, edges, num_bins: int, categorical=(), layout: str = "row",
+             device: int = 0) -> np.ndarray:
+    """Tiled uint8 bins of X (ceil(F/8) * 8 * rows bytes) on `device`."""
+    a = np.ascontiguousarray(np.asarray(X, dtype=np.float32))
+    if a.ndim != 2:
+        raise ValueError(f"X must be 2-dimensional, got shape {a.shape}")
+    if layout == "row":
+        rows, cols = a.shape
+        lay = LAYOUT_ROW_MAJOR
+    else:
+        cols, rows = a.shape
+        lay = LAYOUT_FEATURE_MAJOR
+    e = np.ascontiguousarray(edges, dtype=np.float32)
+    if e.size != cols * (num_bins - 2):
+        raise ValueError(f"edges must hold cols * (num_bins - 2) = {cols * (num_bins - 2)} values")
+    cat = np.zeros(cols, np.uint8)
+    cat[list(categorical)] = 1
+    out = np.empty(((cols + 7) // 8) * 8 * rows, dtype=np.uint8)
+    err = ctypes.c_char_p()
+    if _lib.macboost_bin_data(a.ctypes.data, rows, cols, lay, e.ctypes.data, num_bins,
+                              cat.ctypes.data, device, out.ctypes.data, ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+    return out
+
+
+def predict_tree_binned(bins, rows: int, cols: int, num_bins: int, tree_off, feature, split_bin,
+                        flags, catmask, leaf, max_depth: int, num_classes: int = 1, preds=None,
+                        want_leaf: bool = False, device: int = 0):
+    """predict_tree_binned / assign_leaves for every tree in order: updates the
+    class-major float32 preds (num_classes x rows) in place and returns the
+    tree-major int32 leaf indices (num_trees x rows) when asked."""
+    arrs = [np.ascontiguousarray(bins, np.uint8), np.ascontiguousarray(tree_off, np.int64),
+            np.ascontiguousarray(feature, np.int32), np.ascontiguousarray(split_bin, np.uint32),
+            np.ascontiguousarray(flags, np.uint32), np.ascontiguousarray(catmask, np.uint32),
+            np.ascontiguousarray(leaf, np.float32)]
+    T = len(arrs[1]) - 1
+    if preds is not None and (preds.dtype != np.float32 or not preds.flags.c_contiguous
+                              or preds.size != num_classes * rows):
+        raise ValueError("preds must be a contiguous float32 array of num_classes * rows")
+    li = np.empty((T, rows), np.int32) if want_leaf else None
+    err = ctypes.c_char_p()
+    if _lib.macboost_predict_tree_binned(
+            *[arrs[0].ctypes.data], rows, cols, num_bins, T,
+            *[a.ctypes.data for a in arrs[1:]], max_depth, num_classes, device,
+            preds.ctypes.data if preds is not None else None,
+            li.ctypes.data if li is not None else None, ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+    return li
+
+
+class Dataset:
+    """A MacBoost binned dataset (.mbds) held by the library."""
+
+    def __init__(self, path):
+        err = ctypes.c_char_p()
+        self.ptr = _lib.macboost_dataset_load(str(path).encode(), ctypes.byref(err))
+        if not self.ptr:
+            raise MacBoostError(_take_error(err))
+        self.rows = _lib.macboost_dataset_rows(self.ptr)
+        self.cols = _lib.macboost_dataset_cols(self.ptr)
+        self.num_bins = _lib.macboost_dataset_num_bins(self.ptr)
+
+    def _array(self, fn, dtype, n):
+        out = np.empty(n, dtype)
+        if n:
+            ctypes.memmove(out.ctypes.data, fn(self.ptr), out.nbytes)
+        return out
+
+    @property
+    def bins(self) -> np.ndarray:
+        return self._array(_lib.macboost_dataset_bins, np.uint8,
+                           ((self.cols + 7) // 8) * 8 * self.rows)
+
+    @property
+    def edges(self) -> np.ndarray:
+        return self._array(_lib.macboost_dataset_edges, np.float32,
+                           self.cols * (self.num_bins - 2))
+
+    @property
+    def labels(self) -> np.ndarray:
+        return self._array(_lib.macboost_dataset_labels, np.float32, self.rows)
+
+    @property
+    def categorical(self) -> list[int]:
+        n = _lib.macboost_dataset_num_categorical(self.ptr)
+        return [_lib.macboost_dataset_categorical(self.ptr, i) for i in range(n)]
+
+    @property
+    def feature_names(self) -> list[str] | None:
+        n = _lib.macboost_dataset_num_feature_names(self.ptr)
+        if n < 0:
+            return None
+        return [_lib.macboost_dataset_feature_name(self.ptr, i).decode() for i in range(n)]
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            _lib.macboost_dataset_free(self.ptr)
+            self.ptr = None
+
+
+def predict_dataset(handle: _Handle, dataset: Dataset, kind: int = KIND_PREDICT,
+                    devices=None) -> np.ndarray:
+    """A model's output of `kind` on every row of a binned dataset."""
+    ncol = _lib.macboost_output_cols(handle.ptr, kind)
+    if ncol < 0:
+        raise ValueError(f"unknown output kind {kind}")
+    out = np.empty((dataset.rows, ncol), dtype=np.int32 if kind == KIND_LEAF else np.float32)
+    devs = None
+    nd = 0
+    if devices:
+        devs = (ctypes.c_int32 * len(devices))(*devices)
+        nd = len(devices)
+    err = ctypes.c_char_p()
+    if _lib.macboost_predict_dataset(handle.ptr, dataset.ptr, kind, devs, nd, out.ctypes.data,
+                                     ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+    return out

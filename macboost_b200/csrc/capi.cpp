@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "../../include/macboost_c.h"
+#include "binned.h"
 #include "engine.h"
 #include "table.h"
 
@@ -368,6 +369,132 @@ int32_t macboost_cli_predict(void* handle, const char* data_path, int32_t format
   std::string e;
   if (!mb::cli_predict(*engine(handle), data_path, format, raw != 0, devs, output_path, rows_out,
                        e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+// ---- binned data -----------------------------------------------------------
+
+int32_t macboost_bin_data(const float* x, int64_t rows, int64_t cols, int32_t layout,
+                          const float* edges, int32_t num_bins, const uint8_t* categorical,
+                          int32_t device, uint8_t* bins, char** err) {
+  if ((rows > 0 && cols > 0) && (!x || !bins || (!edges && num_bins > 2))) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::bin_data_host(device, x, rows, cols, layout, edges, num_bins, categorical, bins, e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_predict_tree_binned(const uint8_t* bins, int64_t rows, int64_t cols,
+                                     int32_t num_bins, int32_t num_trees,
+                                     const int64_t* tree_offsets, const int32_t* split_feature,
+                                     const uint32_t* split_bin, const uint32_t* split_flags,
+                                     const uint32_t* cat_mask, const float* leaf_values,
+                                     int32_t max_depth, int32_t num_classes, int32_t device,
+                                     float* preds, int32_t* leaf_idx, char** err) {
+  if (num_trees > 0 && rows > 0 &&
+      (!bins || !tree_offsets || !split_feature || !split_bin || !split_flags || !cat_mask ||
+       !leaf_values)) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::tree_binned_host(device, bins, rows, cols, num_bins, num_trees, tree_offsets,
+                           split_feature, split_bin, split_flags, cat_mask, leaf_values,
+                           max_depth, num_classes, preds, leaf_idx, e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_predict_tree_binned_device(
+    const uint8_t* bins, int64_t rows, int64_t cols, int32_t num_bins, int32_t num_trees,
+    const int64_t* tree_offsets, const int32_t* split_feature, const uint32_t* split_bin,
+    const uint32_t* split_flags, const uint32_t* cat_mask, const float* leaf_values,
+    int32_t max_depth, int32_t num_classes, int32_t device, float* preds, int32_t* leaf_idx,
+    uint32_t* status, void* stream, char** err) {
+  if (num_trees > 0 && rows > 0 &&
+      (!bins || !tree_offsets || !split_feature || !split_bin || !split_flags || !cat_mask ||
+       !leaf_values || !status)) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::tree_binned_device(device, bins, rows, cols, num_bins, num_trees, tree_offsets,
+                             split_feature, split_bin, split_flags, cat_mask, leaf_values,
+                             max_depth, num_classes, preds, leaf_idx, status,
+                             static_cast<cudaStream_t>(stream), e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+void* macboost_dataset_load(const char* path, char** err) {
+  if (!path) {
+    set_error(err, "null path");
+    return nullptr;
+  }
+  auto* d = new (std::nothrow) mb::Dataset();
+  if (!d) {
+    set_error(err, "out of host memory");
+    return nullptr;
+  }
+  std::string e;
+  if (!mb::load_mbds(path, *d, e)) {
+    delete d;
+    set_error(err, e);
+    return nullptr;
+  }
+  return d;
+}
+
+static mb::Dataset* dataset(void* d) { return static_cast<mb::Dataset*>(d); }
+
+int64_t macboost_dataset_rows(void* ds) { return ds ? dataset(ds)->rows : -1; }
+int64_t macboost_dataset_cols(void* ds) { return ds ? dataset(ds)->cols : -1; }
+int32_t macboost_dataset_num_bins(void* ds) { return ds ? dataset(ds)->num_bins : -1; }
+const uint8_t* macboost_dataset_bins(void* ds) { return ds ? dataset(ds)->bins.data() : nullptr; }
+const float* macboost_dataset_edges(void* ds) { return ds ? dataset(ds)->edges.data() : nullptr; }
+const float* macboost_dataset_labels(void* ds) {
+  return ds ? dataset(ds)->labels.data() : nullptr;
+}
+int64_t macboost_dataset_num_categorical(void* ds) {
+  return ds ? int64_t(dataset(ds)->categorical.size()) : -1;
+}
+int64_t macboost_dataset_categorical(void* ds, int64_t i) {
+  if (!ds || i < 0 || i >= int64_t(dataset(ds)->categorical.size())) return -1;
+  return dataset(ds)->categorical[size_t(i)];
+}
+int64_t macboost_dataset_num_feature_names(void* ds) {
+  if (!ds) return -1;
+  return dataset(ds)->has_names ? int64_t(dataset(ds)->names.size()) : -1;
+}
+const char* macboost_dataset_feature_name(void* ds, int64_t i) {
+  if (!ds || !dataset(ds)->has_names || i < 0 || i >= int64_t(dataset(ds)->names.size()))
+    return nullptr;
+  return dataset(ds)->names[size_t(i)].c_str();
+}
+void macboost_dataset_free(void* ds) { delete dataset(ds); }
+
+int32_t macboost_predict_dataset(void* handle, void* ds, int32_t kind, const int32_t* devices,
+                                 int32_t ndev, void* out, char** err) {
+  if (!handle || !ds || (ndev > 0 && !devices) || ndev < 0) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::vector<int> devs(devices, devices + ndev);
+  if (devs.empty()) devs = default_devices();
+  std::string e;
+  if (mb::predict_dataset(*engine(handle), *dataset(ds), kind, devs, out, e)) {
     set_error(err, e);
     return -1;
   }

@@ -100,6 +100,42 @@ size_t shap_smem_bytes(int maxu, bool smem_variant, int S, int R);
 cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas);
 cudaError_t launch_shap(const ShapArgs& a, int maxu, bool smem_variant, size_t smem, int grid,
                         cudaStream_t stream);
+// Binned data (kernels_binned.cu).  Tiled bins as MacBoost's trainer keeps
+// them: bins[(f / 8) * n * 8 + i * 8 + f % 8] for n rows.
+cudaError_t launch_bin_data(const float* x, long long rows, long long cols, long long ld,
+                            int layout, const float* edges, int num_bins,
+                            const unsigned char* categorical, unsigned char* bins,
+                            cudaStream_t stream);
+// Trees in split form (NodeSplit: feature, bin, flags; 8 mask words per node).
+struct BinnedArgs {
+  const unsigned char* bins;
+  long long n;                  // rows
+  long long cols;               // features in the bin matrix
+  int num_bins;
+  int T;
+  const long long* tree_off;    // [T + 1] node offsets
+  const int* feature;
+  const unsigned* sbin;
+  const unsigned* flags;
+  const unsigned* catmask;
+  const float* leaf;
+  int max_depth;
+  int K;
+  // per-tree mode (predict_tree_binned / assign_leaves): class-major preds
+  // (K x n, updated in place) and tree-major leaf indices (T x n); either may be null
+  float* preds;
+  int* leaf_idx;
+  // forest mode (predict on a dataset): margins from `base` in tree order, then
+  // the predict epilogue of output kind `ka.kind` into ka.out (row-major);
+  // kKindLeaf writes row-major leaf indices into ka.out_leaf
+  int forest_mode;
+  const float* base;
+  KArgs ka;
+  unsigned* err;                // kErrBadTree when a split names a missing feature or child
+};
+constexpr unsigned kErrBadTree = 2u;
+cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream);
+
 // Row-major [rows][F] -> feature-major [F][ld] (ld >= rows).
 cudaError_t launch_transpose(const float* in, long long rows, int F, float* out, long long ld,
                              cudaStream_t stream);

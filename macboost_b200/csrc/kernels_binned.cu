@@ -1,0 +1,144 @@
+// sm_100a kernels for binned data: binning raw values into the trainer's
+// tiled bin layout, and walking trees in split form over binned rows.
+//
+// Replaces the Metal kernels bin_data (Sources/MacBoost/Shaders.swift:41-76),
+// predict_tree_binned and assign_leaves (Shaders.swift:1741-1781) with their
+// goes_left rule on a bin (Shaders.swift:466-476).  Layout (bin_index,
+// Shaders.swift:37-39): features in tiles of 8; for n rows, bin (f, i) sits at
+// (f / 8) * n * 8 + i * 8 + f % 8, so the 8 bins of one row and tile are one
+// 8-byte word.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "kernels_common.cuh"
+
+namespace mb {
+namespace {
+
+// One thread per (row, tile of 8 features): the 8 bins packed into one
+// 8-byte store (a warp writes 256 contiguous bytes).
+__global__ void __launch_bounds__(256) bin_data_kernel(const float* __restrict__ x, long long rows,
+                                                       long long cols, long long ld, int layout,
+                                                       const float* __restrict__ edges,
+                                                       int num_bins,
+                                                       const unsigned char* __restrict__ cat,
+                                                       unsigned char* __restrict__ bins) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long g = blockIdx.y;
+  if (i >= rows) return;
+  const unsigned data_bins = unsigned(num_bins) - 1u;
+  unsigned long long packed = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const long long f = g * 8 + k;
+    if (f >= cols) break;
+    const float v = layout == 0 ? __ldg(x + f * ld + i) : __ldg(x + i * cols + f);
+    unsigned b;
+    if (isnan(v)) {
+      b = data_bins;  // the reserved missing bin
+    } else if (__ldg(cat + f) == 1) {
+      // clamp(int(rint(v)), 0, dataBins - 1); the int conversion saturates
+      const float r = rintf(v);
+      b = r < 0.0f ? 0u : (r > float(data_bins - 1) ? data_bins - 1 : unsigned(int(r)));
+    } else {
+      // first upper edge >= v (the reference's binary search, verbatim bounds)
+      const float* e = edges + size_t(f) * (data_bins - 1);
+      unsigned lo = 0, hi = data_bins - 1;
+      while (lo < hi) {
+        const unsigned mid = (lo + hi) >> 1;
+        if (v > __ldg(e + mid))
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      b = lo;
+    }
+    packed |= (unsigned long long)(b & 0xFFu) << (8 * k);
+  }
+  *reinterpret_cast<unsigned long long*>(bins + (g * rows + i) * 8) = packed;
+}
+
+// Final heap index of row i in tree t, walking at most max_depth splits.
+// A split naming a feature outside the matrix or a child outside the tree
+// sets kErrBadTree and ends the walk there.
+__device__ __forceinline__ unsigned walk_binned(const BinnedArgs& a, int t, long long i) {
+  const long long b0 = __ldg(a.tree_off + t);
+  const long long nodes = __ldg(a.tree_off + t + 1) - b0;
+  unsigned node = 0;
+  for (int d = 0; d < a.max_depth; ++d) {
+    const int f = __ldg(a.feature + b0 + node);
+    if (f < 0) break;
+    if (f >= a.cols || 2ll * node + 2 >= nodes) {
+      atomicOr(a.err, kErrBadTree);
+      break;
+    }
+    const unsigned b = a.bins[(size_t(f >> 3) * size_t(a.n) + size_t(i)) * 8 + (f & 7)];
+    const unsigned fl = __ldg(a.flags + b0 + node);
+    bool left;
+    if (fl & 2u)
+      left = (__ldg(a.catmask + (b0 + node) * 8 + (b >> 5)) >> (b & 31)) & 1u;
+    else if (b == unsigned((a.num_bins - 1) & 0xFF))
+      left = (fl & 1u) != 0;
+    else
+      left = b <= (__ldg(a.sbin + b0 + node) & 0xFFu);
+    node = 2 * node + 1 + (left ? 0 : 1);
+  }
+  return node;
+}
+
+template <int KT>
+__global__ void __launch_bounds__(256) binned_kernel(const BinnedArgs a) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    if (!a.forest_mode) {
+      // predict_tree_binned / assign_leaves, one tree after the other
+      for (int t = 0; t < a.T; ++t) {
+        const unsigned node = walk_binned(a, t, i);
+        if (a.preds) a.preds[size_t(t % a.K) * size_t(a.n) + i] += __ldg(a.leaf + __ldg(a.tree_off + t) + node);
+        if (a.leaf_idx) a.leaf_idx[size_t(t) * size_t(a.n) + i] = int(node);
+      }
+      continue;
+    }
+    dev::Acc<KT> acc;
+    acc.init(a.base, a.K);
+    for (int t = 0; t < a.T; ++t) {
+      const unsigned node = walk_binned(a, t, i);
+      if (a.ka.kind == kKindLeaf)
+        a.ka.out_leaf[size_t(i) * a.T + t] = int(node);
+      else
+        acc.add(t, t, __ldg(a.leaf + __ldg(a.tree_off + t) + node));
+    }
+    if (a.ka.kind != kKindLeaf) dev::epilogue<KT>(a.ka, acc, i);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_bin_data(const float* x, long long rows, long long cols, long long ld,
+                            int layout, const float* edges, int num_bins,
+                            const unsigned char* categorical, unsigned char* bins,
+                            cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return cudaSuccess;
+  const dim3 grid(unsigned((rows + 255) / 256), unsigned((cols + 7) / 8));
+  bin_data_kernel<<<grid, 256, 0, stream>>>(x, rows, cols, ld, layout, edges, num_bins,
+                                            categorical, bins);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream) {
+  if (a.n <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = (a.n + 255) / 256;
+  const int grid = int(want < 16ll * sms ? want : 16ll * sms);
+  if (a.forest_mode && a.K == 1)
+    binned_kernel<1><<<grid, 256, 0, stream>>>(a);
+  else
+    binned_kernel<0><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace mb

@@ -457,6 +457,26 @@ bool parse_model_json(const char* text, size_t len, Model& m, std::string& err) 
   return true;
 }
 
+bool parse_json_string_array(const char* text, size_t len, std::vector<std::string>& out,
+                             std::string& err) {
+  out.clear();
+  try {
+    Reader r(text, len);
+    r.expect('[');
+    if (!r.eat(']')) {
+      do {
+        out.push_back(r.str());
+      } while (r.eat(','));
+      r.expect(']');
+    }
+    if (!r.eof()) r.fail("trailing characters");
+    return true;
+  } catch (const ParseError& e) {
+    err = e.what();
+    return false;
+  }
+}
+
 bool load_model_file(const std::string& path, Model& m, std::string& err) {
   FILE* f = std::fopen(path.c_str(), "rb");
   if (!f) {

@@ -67,6 +67,10 @@ struct Model {
 bool load_model_file(const std::string& path, Model& m, std::string& err);
 bool parse_model_json(const char* text, size_t len, Model& m, std::string& err);
 
+// A JSON array of strings (feature-name lists).
+bool parse_json_string_array(const char* text, size_t len, std::vector<std::string>& out,
+                             std::string& err);
+
 // Serialise back to MacBoost JSON (ModelFile keys, Booster.swift:2132-2142).
 std::string model_to_json(const Model& m);
 

@@ -36,7 +36,7 @@ LOG_LINK_OBJECTIVES = (5, 6)   # poisson, tweedie (Booster.swift:15)
 def build(force: bool = False) -> Path:
     """Compile mbref.c and mbshap.c into oracle/libmbref.so with gcc (no
     fast-math, no contraction of multiply-adds)."""
-    srcs = [HERE / "mbref.c", HERE / "mbshap.c"]
+    srcs = [HERE / "mbref.c", HERE / "mbshap.c", HERE / "mbbinned.c"]
     if force or not LIB_PATH.exists() or any(LIB_PATH.stat().st_mtime < s.stat().st_mtime
                                              for s in srcs):
         import subprocess
@@ -62,6 +62,13 @@ def _load():
         lib.mbref_predict.argtypes = [P, ctypes.c_int32, P, P, P, P, P, P, ctypes.c_int32,
                                       ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64,
                                       ctypes.c_int64, ctypes.c_int32, P, P, ctypes.c_int32]
+        lib.mbref_bin_data.restype = ctypes.c_int32
+        lib.mbref_bin_data.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                       ctypes.c_int32, P, ctypes.c_int32, P, P]
+        lib.mbref_predict_binned.restype = ctypes.c_int32
+        lib.mbref_predict_binned.argtypes = [P, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                             P, P, P, P, P, P, ctypes.c_int32, ctypes.c_int32,
+                                             P, P]
         lib.mbref_shap.restype = ctypes.c_int32
         lib.mbref_shap.argtypes = [P, ctypes.c_int32, P, P, P, P, P, P, P, P, ctypes.c_int32,
                                    ctypes.c_int32, P, P, ctypes.c_int64, ctypes.c_int64,
@@ -263,6 +270,108 @@ def shapley_bruteforce(model: OracleModel, x: np.ndarray) -> np.ndarray:
                     Sj = tuple(sorted(S + (j,)))
                     out[k, j] += w * (v[Sj] - v[S])
     return out
+
+
+# ---- binned data (oracle/mbbinned.c restating Shaders.swift:37-76, 1741-1781) ----
+
+def bin_data(X, edges, num_bins: int, categorical, layout: str = "row") -> np.ndarray:
+    """Tiled uint8 bins, ceil(F/8) * 8 * rows bytes (bin_data, Shaders.swift:41-76)."""
+    lib = _load()
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    if layout == "row":
+        rows, cols = X.shape
+        lay, ld = 1, cols
+    else:
+        cols, rows = X.shape
+        lay, ld = 0, rows
+    edges = np.ascontiguousarray(edges, dtype=np.float32)
+    cat = np.zeros(cols, np.uint8)
+    cat[list(categorical)] = 1
+    out = np.empty(((cols + 7) // 8) * 8 * rows, dtype=np.uint8)
+    if lib.mbref_bin_data(_ptr(X), rows, cols, ld, lay, _ptr(edges), num_bins, _ptr(cat),
+                          _ptr(out)) != 0:
+        raise RuntimeError("mbref_bin_data rejected its arguments")
+    return out
+
+
+@dataclass
+class SplitForest:
+    """Trees in the trainer's split form (NodeSplit, Shaders.swift:466)."""
+    tree_off: np.ndarray   # int64[T+1]
+    feature: np.ndarray    # int32[N], < 0 for leaves
+    bin: np.ndarray        # uint32[N]
+    flags: np.ndarray      # uint32[N]
+    catmask: np.ndarray    # uint32[N*8]
+    leaf: np.ndarray       # float32[N]
+
+
+def split_form(model: OracleModel, edges, num_bins: int) -> SplitForest:
+    """A model's trees in split form against a dataset's edges: each numeric
+    threshold is the edge it was trained at (Booster.swift:938 writes
+    threshold = edges[f * (numBins - 2) + bin]); the first matching edge."""
+    ne = num_bins - 2
+    edges = np.asarray(edges, dtype=np.float32).reshape(-1, ne)
+    N = len(model.feature)
+    sb = np.zeros(N, np.uint32)
+    mask = np.zeros(N * 8, np.uint32)
+    for t in range(model.num_trees):
+        for g in range(int(model.tree_off[t]), int(model.tree_off[t + 1])):
+            f = int(model.feature[g])
+            if f < 0:
+                continue
+            if (model.flags[g] & 2) and model.has_mask[t]:
+                mask[g * 8:(g + 1) * 8] = model.catmask[g * 8:(g + 1) * 8]
+                continue
+            hit = np.nonzero(edges[f] == model.threshold[g])[0]
+            if not hit.size:
+                raise ValueError(f"threshold {model.threshold[g]!r} of feature {f} is not a bin edge")
+            sb[g] = hit[0]
+    fl = model.flags.astype(np.uint32).copy()
+    for t in range(model.num_trees):
+        if not model.has_mask[t]:   # a categorical flag without a mask routes numerically
+            a, b = int(model.tree_off[t]), int(model.tree_off[t + 1])
+            fl[a:b] &= ~np.uint32(2)
+    return SplitForest(model.tree_off, model.feature, sb, fl, mask, model.leaf)
+
+
+def predict_binned(bins: np.ndarray, rows: int, num_bins: int, sf: SplitForest, max_depth: int,
+                   K: int = 1, preds: np.ndarray | None = None, want_leaf: bool = False):
+    """predict_tree_binned over every tree in order into class-major preds
+    (K x rows, float32, updated in place) and/or assign_leaves indices (T x rows)."""
+    lib = _load()
+    T = len(sf.tree_off) - 1
+    leaf = np.empty((T, rows), np.int32) if want_leaf else None
+    if lib.mbref_predict_binned(_ptr(np.ascontiguousarray(bins, np.uint8)), rows, num_bins, T,
+                                _ptr(sf.tree_off), _ptr(sf.feature), _ptr(sf.bin),
+                                _ptr(sf.flags), _ptr(sf.catmask), _ptr(sf.leaf), max_depth, K,
+                                _ptr(preds), _ptr(leaf)) != 0:
+        raise RuntimeError("mbref_predict_binned rejected its arguments")
+    return leaf
+
+
+def write_mbds(path, bins, rows: int, cols: int, num_bins: int, categorical, feature_names,
+               edges, labels) -> None:
+    """A .mbds file as BinnedDataset.save writes it (Sources/MacBoost/Dataset.swift:26-39)."""
+    import struct
+    names = json.dumps(feature_names, separators=(",", ":")).encode() if feature_names else b""
+    with open(path, "wb") as fh:
+        fh.write(struct.pack("<III", 0x4D424453, 1, 8))
+        fh.write(struct.pack("<QII", rows, cols, num_bins))
+        cats = sorted(categorical)
+        fh.write(struct.pack("<I", len(cats)))
+        for c in cats:
+            fh.write(struct.pack("<I", c))
+        fh.write(struct.pack("<I", len(names)))
+        fh.write(names)
+        e = np.ascontiguousarray(edges, np.float32)
+        fh.write(struct.pack("<Q", e.size))
+        fh.write(e.tobytes())
+        lab = np.ascontiguousarray(labels, np.float32)
+        fh.write(struct.pack("<Q", lab.size))
+        fh.write(lab.tobytes())
+        b = np.ascontiguousarray(bins, np.uint8)
+        fh.write(struct.pack("<Q", b.size))
+        fh.write(b.tobytes())
 
 
 def predict(model: OracleModel, raw: np.ndarray) -> np.ndarray:
