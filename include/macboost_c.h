@@ -256,6 +256,15 @@ int32_t macboost_bin_data(const float *x, int64_t rows, int64_t cols, int32_t la
                           const float *edges, int32_t num_bins, const uint8_t *categorical,
                           int32_t device, uint8_t *bins, char **err);
 
+/* macboost_bin_data on device memory, enqueued on `stream` (a cudaStream_t;
+ * NULL = legacy default stream) without waiting: x, edges, categorical (cols
+ * flags, required) and bins are device pointers; feature-major x is x[f * ld
+ * + i] with ld >= rows; row-major x ignores ld. */
+int32_t macboost_bin_data_device(const float *x, int64_t rows, int64_t cols, int64_t ld,
+                                 int32_t layout, const float *edges, int32_t num_bins,
+                                 const uint8_t *categorical, int32_t device, uint8_t *bins,
+                                 void *stream, char **err);
+
 /* Walk trees in the trainer's split form over binned rows.  Replaces
  * predict_tree_binned and assign_leaves, Shaders.swift:1741-1781, for
  * num_trees trees at once (one call per finished tree reproduces the

@@ -338,6 +338,25 @@ int bin_data_host(int device, const float* x, int64_t rows, int64_t cols, int la
   return 0;
 }
 
+int bin_data_device(int device, const float* x, int64_t rows, int64_t cols, int64_t ld,
+                    int layout, const float* edges, int num_bins, const uint8_t* categorical,
+                    uint8_t* bins, cudaStream_t stream, std::string& err) {
+  if (rows < 0 || cols < 0 || (layout != 0 && layout != 1) || num_bins < 4 || num_bins > 256 ||
+      (layout == 0 && ld < rows) || !categorical) {
+    err = "invalid argument (rows, cols >= 0; layout 0 or 1 with ld >= rows; num_bins in "
+          "4...256; categorical flags in device memory)";
+    return -1;
+  }
+  if (rows == 0 || cols == 0) return 0;
+  if (check_device(device, err)) return -1;
+  Guard gd(device);
+  BN_CUDA(launch_bin_data(x, rows, cols, layout == 0 ? ld : cols, layout, edges, num_bins,
+                          categorical, bins, stream),
+          "bin_data launch");
+  g_kernel_launches.fetch_add(1);
+  return 0;
+}
+
 namespace {
 
 // Upload trees in split form; validates nothing on the device side (the

@@ -56,6 +56,12 @@ int bin_data_host(int device, const float* x, int64_t rows, int64_t cols, int la
                   const float* edges, int num_bins, const uint8_t* categorical, uint8_t* bins,
                   std::string& err);
 
+// bin_data on device memory, enqueued on `stream` (x feature-major with stride
+// ld, or row-major; categorical: cols device bytes or null).
+int bin_data_device(int device, const float* x, int64_t rows, int64_t cols, int64_t ld,
+                    int layout, const float* edges, int num_bins, const uint8_t* categorical,
+                    uint8_t* bins, cudaStream_t stream, std::string& err);
+
 // predict_tree_binned / assign_leaves for trees 0..T-1 from host memory:
 // preds class-major (K x rows) updated in place, leaf_idx tree-major (T x rows).
 int tree_binned_host(int device, const uint8_t* bins, int64_t rows, int64_t cols, int num_bins,

@@ -392,6 +392,23 @@ int32_t macboost_bin_data(const float* x, int64_t rows, int64_t cols, int32_t la
   return 0;
 }
 
+int32_t macboost_bin_data_device(const float* x, int64_t rows, int64_t cols, int64_t ld,
+                                 int32_t layout, const float* edges, int32_t num_bins,
+                                 const uint8_t* categorical, int32_t device, uint8_t* bins,
+                                 void* stream, char** err) {
+  if ((rows > 0 && cols > 0) && (!x || !bins || !edges)) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::bin_data_device(device, x, rows, cols, ld, layout, edges, num_bins, categorical, bins,
+                          static_cast<cudaStream_t>(stream), e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
 int32_t macboost_predict_tree_binned(const uint8_t* bins, int64_t rows, int64_t cols,
                                      int32_t num_bins, int32_t num_trees,
                                      const int64_t* tree_offsets, const int32_t* split_feature,

@@ -88,6 +88,106 @@ __device__ __forceinline__ unsigned walk_binned(const BinnedArgs& a, int t, long
   return node;
 }
 
+// The same walk reading bins from a staged row tile: tile tb holds, per
+// 8-feature tile g, the R rows' 8-byte words at tb + (g * R + r) * 8.
+__device__ __forceinline__ unsigned walk_staged(const BinnedArgs& a, int t, uint32_t tb, int r,
+                                                int R) {
+  const long long b0 = __ldg(a.tree_off + t);
+  const unsigned nodes = unsigned(__ldg(a.tree_off + t + 1) - b0);
+  const int* feat = a.feature + b0;
+  const unsigned* flags = a.flags + b0;
+  const unsigned* sbin = a.sbin + b0;
+  const uint32_t row = tb + uint32_t(r) * 8u;
+  const uint32_t gstride = uint32_t(R) * 8u;
+  const unsigned last = unsigned((a.num_bins - 1) & 0xFF);
+  unsigned node = 0;
+  for (int d = 0; d < a.max_depth; ++d) {
+    const int f = __ldg(feat + node);
+    if (f < 0) break;
+    if (f >= a.cols || 2u * node + 2u >= nodes) {
+      atomicOr(a.err, kErrBadTree);
+      break;
+    }
+    unsigned b;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(b) : "r"(row + uint32_t(f >> 3) * gstride + uint32_t(f & 7)));
+    const unsigned fl = __ldg(flags + node);
+    bool left;
+    if (fl & 2u)
+      left = (__ldg(a.catmask + (size_t(b0) + node) * 8 + (b >> 5)) >> (b & 31)) & 1u;
+    else if (b == last)
+      left = (fl & 1u) != 0;
+    else
+      left = b <= (__ldg(sbin + node) & 0xFFu);
+    node = 2u * node + (left ? 1u : 2u);
+  }
+  return node;
+}
+
+// Persistent CTAs over row tiles of R = blockDim rows; each tile's bins (one
+// R x 8-byte run per feature tile, 16-byte aligned) arrive by cp.async.bulk,
+// double-buffered on two mbarriers with bounded waits, so the bin matrix is
+// streamed from HBM once and every level of the walk reads shared memory.
+template <int KT, bool FOREST>
+__global__ void __launch_bounds__(256) binned_staged_kernel(const BinnedArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int R = blockDim.x, tid = threadIdx.x;
+  const int groups = int((a.cols + 7) / 8);
+  const uint32_t tile_bytes = uint32_t(groups) * uint32_t(R) * 8u;
+  const uint32_t sbase = dev::smem_u32(smem);
+  const uint32_t bar0 = sbase, buf0 = sbase + 128u;
+  const long long ntiles = (a.n + R - 1) / R;
+  auto issue = [&](long long tile, uint32_t buf) {
+    const long long r0 = tile * R;
+    const long long nr = a.n - r0 < R ? a.n - r0 : R;
+    const uint32_t bytes = uint32_t(((nr + 1) & ~1ll) * 8);  // whole 16-byte units
+    const uint32_t bar = bar0 + 8u * buf;
+    dev::mbar_arrive_expect_tx(bar, bytes * uint32_t(groups));
+    for (int g = 0; g < groups; ++g)
+      dev::bulk_g2s(buf0 + buf * tile_bytes + uint32_t(g) * uint32_t(R) * 8u,
+                    a.bins + (size_t(g) * size_t(a.n) + size_t(r0)) * 8, bytes, bar);
+  };
+  if (tid == 0) {
+    dev::mbar_init(bar0, 1);
+    dev::mbar_init(bar0 + 8, 1);
+    dev::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0 && blockIdx.x < ntiles) issue(blockIdx.x, 0);
+  uint32_t parity = 0;
+  int k = 0;
+  for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
+    const uint32_t buf = uint32_t(k & 1);
+    const bool ok = dev::mbar_wait(bar0 + 8u * buf, (parity >> buf) & 1u, a.err);
+    parity ^= 1u << buf;
+    // all threads are done with the tile in the other buffer: prefetch into it
+    if (__syncthreads_or(!ok)) return;
+    if (tid == 0 && tile + gridDim.x < ntiles) issue(tile + gridDim.x, buf ^ 1u);
+    const long long i = tile * R + tid;
+    if (i < a.n) {
+      const uint32_t tb = buf0 + buf * tile_bytes;
+      if (!FOREST) {
+        for (int t = 0; t < a.T; ++t) {
+          const unsigned node = walk_staged(a, t, tb, tid, R);
+          if (a.preds)
+            a.preds[size_t(t % a.K) * size_t(a.n) + i] += __ldg(a.leaf + __ldg(a.tree_off + t) + node);
+          if (a.leaf_idx) a.leaf_idx[size_t(t) * size_t(a.n) + i] = int(node);
+        }
+      } else {
+        dev::Acc<KT> acc;
+        acc.init(a.base, a.K);
+        for (int t = 0; t < a.T; ++t) {
+          const unsigned node = walk_staged(a, t, tb, tid, R);
+          if (a.ka.kind == kKindLeaf)
+            a.ka.out_leaf[size_t(i) * a.T + t] = int(node);
+          else
+            acc.add(t, t, __ldg(a.leaf + __ldg(a.tree_off + t) + node));
+        }
+        if (a.ka.kind != kKindLeaf) dev::epilogue<KT>(a.ka, acc, i);
+      }
+    }
+  }
+}
+
 template <int KT>
 __global__ void __launch_bounds__(256) binned_kernel(const BinnedArgs a) {
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -132,6 +232,28 @@ cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // staged tiles: every run (g * n + r0) * 8 bytes from a 16-byte aligned base
+  // starts 16-byte aligned when n and R are even; two buffers of R x 8 bytes
+  // per feature tile must fit in shared memory
+  const long long groups = (a.cols + 7) / 8;
+  const int R = 256;
+  const size_t smem = 128 + 2 * size_t(groups) * R * 8;
+  if ((a.n % 2) == 0 && (reinterpret_cast<uintptr_t>(a.bins) % 16) == 0 && groups > 0 &&
+      smem <= 200 * 1024) {
+    const long long ntiles = (a.n + R - 1) / R;
+    void (*k)(const BinnedArgs) = !a.forest_mode ? binned_staged_kernel<1, false>
+                                  : a.K == 1     ? binned_staged_kernel<1, true>
+                                                 : binned_staged_kernel<0, true>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return e;
+    int per_sm = 1;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, R, smem);
+    if (e != cudaSuccess) return e;
+    const long long want = (long long)(per_sm < 1 ? 1 : per_sm) * sms;
+    const int grid = int(ntiles < want ? ntiles : want);
+    k<<<grid, R, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
   const long long want = (a.n + 255) / 256;
   const int grid = int(want < 16ll * sms ? want : 16ll * sms);
   if (a.forest_mode && a.K == 1)
