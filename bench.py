@@ -298,11 +298,24 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--ref-rows", type=int, default=200_000)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="predict", choices=["predict", "contrib", "binned"],
+                    help="predict: the headline (forest predict); contrib: TreeSHAP "
+                         "contributions; binned: one tree walked over binned rows per step, "
+                         "as a trainer evaluates each new tree, plus bin_data")
+    ap.add_argument("--trees", type=int, default=0, help="override the model's tree count")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     dist = Dist()
     cfg = synth.CONFIGS[args.config]
+    if args.workload == "contrib":
+        run_contrib(args, dist, cfg)
+        dist.close()
+        return
+    if args.workload == "binned":
+        run_binned(args, dist, cfg)
+        dist.close()
+        return
     text = synth.model_to_json(synth.make_model(cfg))
 
     if args.impl == "reference":
@@ -422,6 +435,219 @@ def main():
         print(json.dumps(line), flush=True)
     del xd, outd
     dist.close()
+
+
+def _time_steps(step, steps, warmup, stream, dist, clocks=None):
+    """Device time of `steps` launches on `stream` (ms, max over ranks)."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    if clocks:
+        clocks.sample()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    clk = clocks.stop() if clocks else None
+    return dist.max(ms_local), ms_local, clk
+
+
+CONTRIB_ROWS = {"cfg1": 500_000, "cfg2": 1_000_000, "cfg3": 500_000, "cfg4": 100_000,
+                "cfg5": 100_000}
+
+
+def run_contrib(args, dist, cfg):
+    """--workload contrib: TreeSHAP contributions (macboost_predict_contrib_device) on
+    the config's model with node covers from 20,000 routed rows, device-resident
+    feature-major input; e2e through macboost_predict_contrib_ex on pinned buffers."""
+    import torch
+
+    from macboost_b200 import _core
+    dev = dist.local_rank
+    torch.cuda.set_device(dev)
+    rows = args.rows or CONTRIB_ROWS[cfg.name]
+    trees = args.trees or cfg.trees
+    model = synth.make_model(cfg, trees=trees)
+    synth.add_covers(model, synth.make_data(cfg, rows=20_000, seed=cfg.data_seed + 7,
+                                            layout="row"))
+    text = synth.model_to_json(model)
+    h = _core.load_json(text)
+    _core.prepare(h, [dev])
+    F, K = cfg.features, cfg.classes
+    W = K * (F + 1)
+    Xh = _core.pinned_empty((F, rows))
+    synth.make_data(cfg, rows=rows, row_start=dist.rank * rows, layout="feature", out=Xh)
+    xd = torch.from_numpy(np.asarray(Xh)).to(f"cuda:{dev}")
+    outd = torch.empty((rows, W), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        _core.predict_contrib_device(h, dev, xd.data_ptr(), rows, F, rows, outd.data_ptr(),
+                                     stream=stream.cuda_stream)
+
+    launches0 = _core.kernel_launches()
+    ms, ms_local, clk = _time_steps(step, args.steps, args.warmup, stream, dist,
+                                    ClockSampler(dev))
+    launches = _core.kernel_launches() - launches0 - args.warmup
+    _core.check_device(h, dev)
+    per_step = ms / 1e3 / args.steps
+    units = rows * trees * dist.world
+    e2e = None
+    if args.e2e_steps > 0:
+        outh = _core.pinned_empty((rows, W))
+        ts = []
+        for _ in range(args.e2e_steps + 1):
+            dist.barrier()
+            t0 = time.perf_counter()
+            _core.predict_contrib_ex(h, np.asarray(Xh), layout="feature", devices=[dev])
+            ts.append(time.perf_counter() - t0)
+        e2e_s = dist.max(sum(ts[1:]) / len(ts[1:]))
+        e2e = {"value": units / e2e_s, "unit": UNIT, "h2d_bytes_per_step": rows * F * 4,
+               "d2h_bytes_per_step": rows * W * 4}
+        del outh
+    peak, peak_src = measured_peak_hbm()
+    alg = rows * 4 * (F + W)
+    line = {
+        "metric": "TreeSHAP contributions rows·trees/s", "value": units / per_step,
+        "unit": UNIT, "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded model and rows)",
+        "config": {"workload": f"contrib on {cfg.name}: {rows} rows x {trees} trees, "
+                               f"covers from 20,000 routed rows",
+                   "rows_per_gpu": rows, "features": F, "trees": trees, "classes": K,
+                   "output": "rows x K x (F+1) float32",
+                   "l2": "inputs and outputs larger than L2" if alg > (126 << 20)
+                         else "output written once per step"},
+        "roofline": {"bound": "hbm", "achieved": alg / (ms_local / 1e3 / args.steps) / 1e9,
+                     "peak": peak, "unit": "GB/s", "peak_source": peak_src,
+                     "frac": alg / (ms_local / 1e3 / args.steps) / 1e9 / peak,
+                     "traffic": None, "algorithmic_bytes_per_launch": alg,
+                     "note": "float64 path arithmetic bound (latency and occupancy), "
+                             "not HBM: bytes = input values + contribution outputs"},
+        "e2e": e2e, "gpu_launches": int(launches), "clocks": clk,
+    }
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.build()
+        om = O.model_from_dict(json.loads(text))
+        n = 256 if trees * cfg.features <= 20_000 else 64
+        Xs = synth.make_data(cfg, rows=n, seed=cfg.data_seed + 99, layout="row")
+        t0 = time.perf_counter()
+        O.predict_contrib(om, Xs)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {
+            "value": n * trees / dt, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{n} rows x {trees} trees, {dt:.2f} s (oracle/mbshap.c, restatement "
+                      f"of SHAP.swift's recursive CPU TreeSHAP)"}
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    del xd, outd
+
+
+def run_binned(args, dist, cfg):
+    """--workload binned: per step, one depth-6 tree in split form walked over the
+    config's rows in the trainer's tiled bin layout (predict_tree_binned + its leaf
+    indices, device memory), as a trainer evaluates each new tree; the line also
+    times bin_data on the same rows."""
+    import ctypes
+
+    import torch
+
+    from macboost_b200 import _core
+    dev = dist.local_rank
+    torch.cuda.set_device(dev)
+    rows = (args.rows or cfg.rows) // 2 * 2
+    F, nb, depth = cfg.features, 256, 6
+    groups = (F + 7) // 8
+    rng = np.random.default_rng(cfg.model_seed + 11)
+    n_nodes = (1 << (depth + 1)) - 1
+    feat = np.full(n_nodes, -1, np.int32)
+    feat[: (1 << depth) - 1] = rng.integers(0, F, (1 << depth) - 1)
+    sbin = rng.integers(0, nb - 2, n_nodes).astype(np.uint32)
+    flags = rng.integers(0, 2, n_nodes).astype(np.uint32)
+    leaf = rng.standard_normal(n_nodes).astype(np.float32)
+    g = torch.Generator(device=f"cuda:{dev}").manual_seed(cfg.data_seed)
+    bins = torch.randint(0, nb, (groups * 8 * rows,), dtype=torch.uint8, device=f"cuda:{dev}",
+                         generator=g)
+    d = {k: torch.from_numpy(v).to(f"cuda:{dev}") for k, v in
+         (("off", np.array([0, n_nodes], np.int64)), ("feat", feat), ("sbin", sbin.view(np.int32)),
+          ("flags", flags.view(np.int32)), ("mask", np.zeros(n_nodes * 8, np.int32)),
+          ("leaf", leaf))}
+    preds = torch.zeros(rows, dtype=torch.float32, device=f"cuda:{dev}")
+    leafidx = torch.empty(rows, dtype=torch.int32, device=f"cuda:{dev}")
+    status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+    stream = torch.cuda.current_stream(dev)
+    lib = _core._lib
+    P, I32, I64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    fn = lib.macboost_predict_tree_binned_device
+    fn.restype = I32
+    fn.argtypes = [P, I64, I64, I32, I32, P, P, P, P, P, P, I32, I32, I32, P, P, P, P,
+                   ctypes.POINTER(ctypes.c_char_p)]
+    err = ctypes.c_char_p()
+
+    def step():
+        if fn(bins.data_ptr(), rows, F, nb, 1, d["off"].data_ptr(), d["feat"].data_ptr(),
+              d["sbin"].data_ptr(), d["flags"].data_ptr(), d["mask"].data_ptr(),
+              d["leaf"].data_ptr(), depth, 1, dev, preds.data_ptr(), leafidx.data_ptr(),
+              status.data_ptr(), stream.cuda_stream, ctypes.byref(err)) != 0:
+            raise RuntimeError(err.value)
+
+    launches0 = _core.kernel_launches()
+    ms, ms_local, clk = _time_steps(step, args.steps, args.warmup, stream, dist,
+                                    ClockSampler(dev))
+    launches = _core.kernel_launches() - launches0 - args.warmup
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    # bin_data on the config's rows (device-resident, feature-major)
+    x = torch.from_numpy(synth.make_data(cfg, rows=rows, layout="feature")).to(f"cuda:{dev}")
+    edges = torch.from_numpy(np.sort(rng.standard_normal((F, nb - 2)), axis=1)
+                             .astype(np.float32)).to(f"cuda:{dev}")
+    cat = torch.zeros(F, dtype=torch.uint8, device=f"cuda:{dev}")
+    fb = lib.macboost_bin_data_device
+    fb.restype = I32
+    fb.argtypes = [P, I64, I64, I64, I32, P, I32, P, I32, P, P, ctypes.POINTER(ctypes.c_char_p)]
+
+    def bstep():
+        if fb(x.data_ptr(), rows, F, rows, 0, edges.data_ptr(), nb, cat.data_ptr(), dev,
+              bins.data_ptr(), stream.cuda_stream, ctypes.byref(err)) != 0:
+            raise RuntimeError(err.value)
+
+    bms, bms_local, _ = _time_steps(bstep, args.steps, args.warmup, stream, dist)
+    peak, peak_src = measured_peak_hbm()
+    per_row = groups * 8 + 4 + 4 + 4          # tile words + preds read/write + leaf index
+    t_step = ms_local / 1e3 / args.steps
+    line = {
+        "metric": "binned tree walk rows·trees/s", "value": rows * dist.world / (ms / 1e3 / args.steps),
+        "unit": UNIT, "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (random bins and tree)",
+        "config": {"workload": f"binned on {cfg.name}: {rows} rows x {F} features "
+                               f"({groups} tiles of 8), one depth-6 tree per step, "
+                               f"predict_tree_binned + assign_leaves",
+                   "rows_per_gpu": rows, "features": F, "trees": 1, "num_bins": nb,
+                   "l2": "bin matrix larger than L2 (streamed once per step)"},
+        "roofline": {"bound": "hbm", "achieved": rows * per_row / t_step / 1e9, "peak": peak,
+                     "unit": "GB/s", "peak_source": peak_src,
+                     "frac": rows * per_row / t_step / 1e9 / peak, "traffic": None,
+                     "algorithmic_bytes_per_launch": rows * per_row,
+                     "note": "bytes = the rows' tile words + preds read/write + leaf index"},
+        "bin_data": {"ms_per_step": bms / args.steps,
+                     "achieved_gbs": rows * F * 5 / (bms_local / 1e3 / args.steps) / 1e9,
+                     "note": "reads F x 4 B values, writes F bin bytes per row"},
+        "e2e": None, "gpu_launches": int(launches), "clocks": clk,
+    }
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -140,6 +140,16 @@ int32_t macboost_predict_contrib_ex(void *handle, const float *x, int64_t rows, 
                                     int32_t layout, const int32_t *devices, int32_t ndev,
                                     float *out, char **err);
 
+/* TreeSHAP contributions from device memory on `device`, enqueued on `stream`
+ * (a cudaStream_t; NULL = legacy default stream): x_dev as in
+ * macboost_predict_device, out_dev rows x K x (cols + 1) floats.  Row-major
+ * input, and models whose accumulators do not fit in shared memory, make the
+ * call wait for its work; otherwise kernel-side errors are reported by
+ * macboost_check_device. */
+int32_t macboost_predict_contrib_device(void *handle, int32_t device, const float *x_dev,
+                                        int64_t rows, int64_t cols, int64_t ld, int32_t layout,
+                                        float *out_dev, void *stream, char **err);
+
 /* Upload the model to the listed devices now (otherwise done on first use). */
 int32_t macboost_prepare(void *handle, const int32_t *devices, int32_t ndev, char **err);
 

@@ -71,6 +71,8 @@ def _configure(lib):
         "macboost_host_free": (None, [P]),
         "macboost_predict_contrib": (I32, [P, _f32_p, I64, I64, _f32_p, _c_char_pp]),
         "macboost_predict_contrib_ex": (I32, [P, P, I64, I64, I32, _i32_p, I32, P, _c_char_pp]),
+        "macboost_predict_contrib_device": (I32, [P, I32, P, I64, I64, I64, I32, P, P,
+                                                  _c_char_pp]),
         "macboost_bin_data": (I32, [P, I64, I64, I32, P, I32, P, I32, P, _c_char_pp]),
         "macboost_predict_tree_binned": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P, I32,
                                                I32, I32, P, P, _c_char_pp]),
@@ -272,6 +274,17 @@ def predict_contrib_ex(handle: _Handle, X, layout: str = "row", devices=None) ->
     if rc != 0:
         raise MacBoostError(_take_error(err))
     return out
+
+
+def predict_contrib_device(handle: _Handle, device: int, x_ptr: int, rows: int, cols: int,
+                           ld: int, out_ptr: int, layout: int = LAYOUT_FEATURE_MAJOR,
+                           stream: int = 0) -> None:
+    """Enqueue SHAP contributions on device buffers (raw pointers) on `stream`."""
+    err = ctypes.c_char_p()
+    rc = _lib.macboost_predict_contrib_device(handle.ptr, device, x_ptr, rows, cols, ld, layout,
+                                              out_ptr, stream or None, ctypes.byref(err))
+    if rc != 0:
+        raise MacBoostError(_take_error(err))
 
 
 def predict_ex(handle: _Handle, X, kind: int = KIND_PREDICT, layout: str = "row",

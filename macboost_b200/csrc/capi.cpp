@@ -294,6 +294,22 @@ int32_t macboost_predict_contrib_ex(void* handle, const float* x, int64_t rows, 
   return 0;
 }
 
+int32_t macboost_predict_contrib_device(void* handle, int32_t device, const float* x_dev,
+                                        int64_t rows, int64_t cols, int64_t ld, int32_t layout,
+                                        float* out_dev, void* stream, char** err) {
+  if (!handle || !x_dev || !out_dev) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (mb::engine_contrib_device(*engine(handle), device, x_dev, rows, cols, ld, layout, out_dev,
+                                static_cast<cudaStream_t>(stream), e) != 0) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
 int64_t macboost_num_feature_names(void* handle) {
   if (!handle) return -1;
   const mb::Model& m = engine(handle)->model;

@@ -630,6 +630,41 @@ int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
   return 0;
 }
 
+// Enqueue the contributions kernel over `rows` rows of feature-major x
+// (stride ld; slot_map null: x holds the staged slots in order).
+int launch_shap_on(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
+                   const int* slot_map, float* out, cudaStream_t st, std::string& err) {
+  const ShapForest& s = e.shap;
+  ShapArgs a{};
+  a.x = x;
+  a.rows = rows;
+  a.ld = ld;
+  a.slot_map = slot_map;
+  a.S = int(s.slot_feature.size());
+  a.paths = d.shap_paths;
+  a.uniq = d.shap_uniq;
+  a.masks = d.shap_masks;
+  a.block_path = d.shap_block_path;
+  a.block_uniq = d.shap_block_uniq;
+  a.class_block = d.shap_class_block;
+  a.err = d.err;
+  a.coef = d.shap_coef;
+  a.feature_slot = d.shap_feature_slot;
+  a.bias = d.shap_bias;
+  a.K = e.model.K;
+  a.F = int(e.model.num_features);
+  a.data_bins = e.model.num_bins - 1;
+  a.out = out;
+  a.scratch = d.shap_scratch;
+  a.R = d.shap_R;
+  a.ntiles = (rows + a.R - 1) / a.R;
+  const int grid = int(std::min<int64_t>(d.shap_grid, a.ntiles));
+  MB_CUDA(launch_shap(a, std::max(s.max_unique, 1), d.shap_in_smem, d.shap_smem, grid, st),
+          "contributions kernel launch");
+  g_kernel_launches.fetch_add(1);
+  return 0;
+}
+
 // One GPU's share [r_begin, r_end) of a host-memory contributions call:
 // double-buffered chunks as in run_slice (H2D of the used feature columns,
 // kernel, D2H of the chunk's rows x K x (F + 1) block).
@@ -700,33 +735,9 @@ int run_contrib_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, i
       MB_CUDA(launch_transpose(d.xraw[p], nr, int(cols), d.xbuf[p], ldc, st), "transpose launch");
       slot_map = d.shap_slot_feature;
     }
-    ShapArgs a{};
-    a.x = d.xbuf[p];
-    a.rows = nr;
-    a.ld = ldc;
-    a.slot_map = slot_map;
-    a.S = S;
-    a.paths = d.shap_paths;
-    a.uniq = d.shap_uniq;
-    a.masks = d.shap_masks;
-    a.block_path = d.shap_block_path;
-    a.block_uniq = d.shap_block_uniq;
-    a.class_block = d.shap_class_block;
-    a.err = d.err;
-    a.coef = d.shap_coef;
-    a.feature_slot = d.shap_feature_slot;
-    a.bias = d.shap_bias;
-    a.K = K;
-    a.F = int(cols);
-    a.data_bins = e.model.num_bins - 1;
-    a.out = static_cast<float*>(d.obuf[p]);
-    a.scratch = d.shap_scratch;
-    a.R = R;
-    a.ntiles = (nr + R - 1) / R;
-    const int grid = int(std::min<int64_t>(d.shap_grid, a.ntiles));
-    MB_CUDA(launch_shap(a, std::max(s.max_unique, 1), d.shap_in_smem, d.shap_smem, grid, st),
-            "contributions kernel launch");
-    g_kernel_launches.fetch_add(1);
+    if (launch_shap_on(e, d, d.xbuf[p], nr, ldc, slot_map, static_cast<float*>(d.obuf[p]), st,
+                       err))
+      return -1;
     if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
     prev_r0 = r0;
     prev_n = nr;
@@ -739,6 +750,57 @@ int run_contrib_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, i
 }
 
 }  // namespace
+
+int engine_contrib_device(Engine& e, int device, const float* x, int64_t rows, int64_t cols,
+                          int64_t ld, int layout, float* out, cudaStream_t stream,
+                          std::string& err) {
+  if (rows < 0) {
+    err = "rows must be >= 0";
+    return -1;
+  }
+  if (cols != e.model.num_features) {
+    err = "model expects " + std::to_string(e.model.num_features) + " features, got " +
+          std::to_string(cols);
+    return -1;
+  }
+  if (layout != 0 && layout != 1) {
+    err = "layout must be 0 (feature-major) or 1 (row-major)";
+    return -1;
+  }
+  if (layout == 0 && ld < rows) {
+    err = "feature-major input needs ld >= rows";
+    return -1;
+  }
+  if (!ensure_shap_built(e, err)) return -1;
+  if (rows == 0) return 0;
+  if (!x || !out) {
+    err = "null argument";
+    return -1;
+  }
+  DeviceState* d = engine_prepare(e, device, err);
+  if (!d) return -1;
+  std::lock_guard<std::mutex> lk(d->mu);
+  DeviceGuard g(device);
+  if (prepare_shap(e, *d, err)) return -1;
+  bool wait = !d->shap_in_smem;  // the global accumulators are one region per device
+  if (layout == 0) {
+    if (launch_shap_on(e, *d, x, rows, ld, d->shap_slot_feature, out, stream, err)) return -1;
+  } else {
+    const int64_t ldt = (rows + 3) / 4 * 4;
+    if (ensure(reinterpret_cast<void*&>(d->xbuf[0]), d->xcap[0],
+               size_t(std::max<int64_t>(cols, 1)) * ldt * 4, err))
+      return -1;
+    MB_CUDA(launch_transpose(x, rows, int(cols), d->xbuf[0], ldt, stream), "transpose launch");
+    if (launch_shap_on(e, *d, d->xbuf[0], rows, ldt, d->shap_slot_feature, out, stream, err))
+      return -1;
+    wait = true;  // the staging buffer is private to this call
+  }
+  if (wait) {
+    MB_CUDA(cudaStreamSynchronize(stream), "contributions");
+    return check_err_word(*d, err);
+  }
+  return 0;
+}
 
 int engine_contrib_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
                         const std::vector<int>& devices_in, float* out, std::string& err) {

@@ -105,6 +105,13 @@ int engine_predict_device(Engine& e, int device, const float* x, int64_t rows, i
 int engine_contrib_host(Engine& e, const float* x, int64_t rows, int64_t cols, int layout,
                         const std::vector<int>& devices, float* out, std::string& err);
 
+// TreeSHAP contributions from device memory on `device`, enqueued on
+// `stream` (feature-major x[f * ld + i], or row-major; row-major input and
+// models too wide for shared-memory accumulators make the call wait).
+int engine_contrib_device(Engine& e, int device, const float* x, int64_t rows, int64_t cols,
+                          int64_t ld, int layout, float* out, cudaStream_t stream,
+                          std::string& err);
+
 // Synchronise `device` and report any kernel-side error since the last check.
 int engine_check_device(Engine& e, int device, std::string& err);
 
