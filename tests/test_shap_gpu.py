@@ -145,3 +145,33 @@ def test_contrib_multi_device(gpu, oracle_built):
     one = core.predict_contrib_ex(h, X, devices=[0])
     many = core.predict_contrib_ex(h, X, devices=list(range(min(n, 4))))
     assert np.array_equal(one.view(np.uint32), many.view(np.uint32))
+
+
+def test_contrib_device_entry_point(gpu, oracle_built):
+    """macboost_predict_contrib_device on device buffers (feature-major with a
+    padded stride, and row-major) equals the host-memory call bit for bit."""
+    core = gpu
+    from test_gpu_parity import _cudart
+    cu = _cudart()
+    text, om = covered("cfg3", 40)
+    h = core.load_json(text)
+    rows, F = 3001, om.num_features
+    X = synth.make_data("cfg3", rows=rows, row_start=9, layout="row")
+    want = core.predict_contrib_ex(h, X)
+    W = want.shape[1]
+    ld = 3008
+    fm = np.zeros((F, ld), np.float32)
+    fm[:, :rows] = X.T
+    for src, layout, stride in ((fm, core.LAYOUT_FEATURE_MAJOR, ld),
+                                (np.ascontiguousarray(X), core.LAYOUT_ROW_MAJOR, F)):
+        dx = cu.alloc(src.nbytes)
+        dout = cu.alloc(rows * W * 4)
+        try:
+            cu.h2d(dx, src)
+            core.predict_contrib_device(h, 0, dx, rows, F, stride, dout, layout=layout)
+            core.check_device(h, 0)
+            got = cu.d2h(dout, rows * W, np.float32).reshape(rows, W)
+        finally:
+            cu.free(dx)
+            cu.free(dout)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"layout {layout}"
