@@ -126,7 +126,7 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = int(std::min<int64_t>(a.ntiles, d.grid_ctas));
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
-                                 e.flat.plan.smem, grid, s, e.flat.code_bytes);
+                                 e.flat.plan.smem, grid, s, e.flat.code_bytes, e.top.get());
   if (ce != cudaSuccess) {
     err = cuda_msg("forest kernel launch", ce);
     return -1;
@@ -169,6 +169,11 @@ static Engine* finish_load(Engine* e, std::string& err) {
     return nullptr;
   }
   e->description = describe_forest(e->flat);
+  if (!e->flat.top_recs.empty() && !e->flat.codes && e->flat.layout == Layout::kComplete) {
+    e->top = std::make_unique<TopRecords>();
+    std::memset(e->top.get(), 0, sizeof(TopRecords));
+    std::memcpy(e->top->rec, e->flat.top_recs.data(), e->flat.top_recs.size() * 8);
+  }
   return e;
 }
 
@@ -266,7 +271,8 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
     }
   int ctas = 0;
   ce = forest_occupancy(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, e.flat.K,
-                        e.flat.G, e.flat.plan.R, e.flat.plan.smem, &ctas, e.flat.code_bytes);
+                        e.flat.G, e.flat.plan.R, e.flat.plan.smem, &ctas, e.flat.code_bytes,
+                        e.top != nullptr);
   if (ce != cudaSuccess || ctas < 1) {
     err = ce != cudaSuccess ? cuda_msg("occupancy query", ce)
                             : std::string("the forest kernel cannot be resident on an SM");
@@ -530,7 +536,7 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = int(std::min<int64_t>(a.ntiles, d->grid_ctas));
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
-                                 e.flat.plan.smem, grid, stream, e.flat.code_bytes);
+                                 e.flat.plan.smem, grid, stream, e.flat.code_bytes, e.top.get());
   if (ce != cudaSuccess) {
     err = cuda_msg("forest kernel launch", ce);
     return -1;

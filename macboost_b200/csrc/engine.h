@@ -69,6 +69,7 @@ struct DeviceState {
 struct Engine {
   Model model;
   FlatForest flat;
+  std::unique_ptr<TopRecords> top;      // complete layout: first two levels as a kernel parameter
   std::string description;
   std::mutex mu;                        // guards `devices`
   std::map<int, std::unique_ptr<DeviceState>> devices;

@@ -1,6 +1,8 @@
 // Forest flattening and launch planning (layouts described in forest.h).
 #include "forest.h"
 
+#include "kernels.h"
+
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -35,7 +37,7 @@ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Optional restriction of the planner's choices from the environment, for
 // tuning: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0" (any subset; 0 = free).
 struct PlanOverride {
-  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1;
+  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
     if (!s) return;
@@ -51,6 +53,7 @@ struct PlanOverride {
       else if (key == "bufs") bufs = int(v);
       else if (key == "planes") planes = int(v);
       else if (key == "codes") codes = int(v);
+      else if (key == "top") top = int(v);
       p = end;
       while (*p == ',' || *p == ' ') ++p;
     }
@@ -453,6 +456,24 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
       fill(0, 0, -1, 0);
       f.nodes += int64_t(NL) * 2 - 1;
     }
+    // Heap nodes 0, 1, 2 (slots 1, 2, 3) of every tree for the kernel
+    // parameter.  It removes the first two levels' shared-memory record loads,
+    // which pays where those loads bound the walk: with NaN planes (one compare
+    // per node).  Without planes the walk is bound by ALU issue (flag test and
+    // compare select per node) and the constant-bank reads and selects only add
+    // to it (B200: cfg2 2.4% faster with, cfg1/cfg3 4.5% slower).
+    const PlanOverride ov;
+    if (D >= 2 && f.Tpad <= kTopTrees && ov.top != 0 && (f.plan.planes || ov.top == 1)) {
+      f.top_recs.resize(size_t(f.Tpad) * 3);
+      for (int t = 0; t < f.Tpad; ++t) {
+        const int b = t / Tb, i = t % Tb;
+        const auto* slots = reinterpret_cast<const uint2_like*>(f.blob.data() + f.block_off[size_t(b)]) +
+                            size_t(i) * NL;
+        for (int k = 0; k < 3; ++k)
+          f.top_recs[size_t(t) * 3 + size_t(k)] =
+              uint64_t(slots[k + 1].x) | (uint64_t(slots[k + 1].y) << 32);
+      }
+    }
   } else {
     f.leaf_heap.assign(node_prefix.back(), -1);
     f.block_rec_base.assign(size_t(nb), 0);
@@ -533,6 +554,7 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"tile_slots\":" + std::to_string(f.S_total);
   s += ",\"nan_planes\":" + std::string(f.plan.planes ? "true" : "false");
   s += ",\"codes\":" + std::string(f.codes ? "true" : "false");
+  s += ",\"top_params\":" + std::string(f.top_recs.empty() ? "false" : "true");
   if (f.codes) {
     s += ",\"code_bytes\":" + std::to_string(f.code_bytes);
     s += ",\"code_slots\":" + std::to_string(f.S_code);

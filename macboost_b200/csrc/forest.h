@@ -127,6 +127,10 @@ struct FlatForest {
   uint32_t leaf_off = 0;               // complete layout: leaves offset in a block
   int max_depth = 0;
   int64_t nodes = 0;
+  // complete layout: records of heap nodes 0, 1, 2 of each padded tree (3 per
+  // tree, x | y << 32), passed to the kernel as a parameter; empty when the
+  // forest is deeper than it allows (more than kTopTrees trees, or D < 2)
+  std::vector<uint64_t> top_recs;
   uint32_t neg_inf_slot_bytes = 0xFFFFFFFFu;  // explicit: tile offset of the -Inf slot
 
   // Binned-code layout (see forest_codes.cpp): each staged value becomes its

@@ -28,19 +28,24 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
 }  // namespace
 
 cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,
-                          int grid, cudaStream_t stream, int code_bytes) {
+                          int grid, cudaStream_t stream, int code_bytes, const TopRecords* top) {
   if (layout == 2) return launch_codes(code_bytes, cat, a, smem, grid, stream, nullptr);
+  if (layout == 0 && top) return launch_complete_top(planes, cat, a, *top, smem, grid, stream, nullptr);
   return layout == 0 ? launch_complete(planes, cat, a, smem, grid, stream, nullptr)
                      : launch_explicit(planes, cat, a, smem, grid, stream, nullptr);
 }
 
 cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
-                             size_t smem, int* ctas, int code_bytes) {
+                             size_t smem, int* ctas, int code_bytes, bool top) {
   KArgs a{};
   a.K = K;
   a.G = G;
   a.R = R;
   if (layout == 2) return launch_codes(code_bytes, cat, a, smem, 1, nullptr, ctas);
+  if (layout == 0 && top) {
+    static TopRecords none{};
+    return launch_complete_top(planes, cat, a, none, smem, 1, nullptr, ctas);
+  }
   return layout == 0 ? launch_complete(planes, cat, a, smem, 1, nullptr, ctas)
                      : launch_explicit(planes, cat, a, smem, 1, nullptr, ctas);
 }

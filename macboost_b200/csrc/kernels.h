@@ -60,15 +60,26 @@ struct KArgs {
   unsigned* err;
 };
 
+// Complete layout: the records of heap nodes 0, 1 and 2 of every tree, passed
+// by value as a kernel parameter, so the first two levels of the walk read the
+// constant bank (uniform per warp) instead of shared memory.  Record of node k
+// of tree t at rec[3 t + k], as the 8-byte shared-memory record (x | y << 32).
+constexpr int kTopTrees = 1200;
+struct TopRecords {
+  unsigned long long rec[3 * kTopTrees];
+};
+
 // Launch the forest kernel on `stream`.  layout: 0 complete, 1 explicit,
 // 2 complete with binned codes (code_bytes 1 or 2); planes: NaN planes in the
-// tile; cat: the model has categorical splits.
+// tile; cat: the model has categorical splits; top (complete layout only):
+// the first two levels' records, or null to read every level from shared memory.
 cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,
-                          int grid, cudaStream_t stream, int code_bytes = 1);
+                          int grid, cudaStream_t stream, int code_bytes = 1,
+                          const TopRecords* top = nullptr);
 
 // Largest number of co-resident CTAs per SM for that kernel.
 cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
-                             size_t smem, int* ctas, int code_bytes = 1);
+                             size_t smem, int* ctas, int code_bytes = 1, bool top = false);
 
 // TreeSHAP contributions (kernels_shap.cu).  Rows: feature-major
 // x[slot_map[s] * ld + i] (x[s * ld + i] when slot_map is null) for the S

@@ -362,6 +362,8 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
 // Per-layout launchers (kernels_complete.cu, kernels_explicit.cu, kernels_codes.cu).
 cudaError_t launch_codes(int code_bytes, bool cat, const KArgs& a, size_t smem, int grid,
                          cudaStream_t stream, int* occupancy_out);
+cudaError_t launch_complete_top(bool planes, bool cat, const KArgs& a, const TopRecords& top,
+                                size_t smem, int grid, cudaStream_t stream, int* occupancy_out);
 cudaError_t launch_complete(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
                             cudaStream_t stream, int* occupancy_out);
 cudaError_t launch_explicit(bool planes, bool cat, const KArgs& a, size_t smem, int grid,

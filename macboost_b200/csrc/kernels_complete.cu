@@ -32,15 +32,23 @@
 // Tensor cores are not used: tree traversal is a data-dependent walk, not a
 // dense contraction.  Every mbarrier wait is bounded (globaltimer); on expiry
 // the CTA records kErrWaitTimeout in *err and all its threads return together.
+#include <type_traits>
+
 #include "kernels_common.cuh"
 
 namespace mb {
 namespace {
 
-template <int KT, int G, bool PLANES, bool CAT>
-__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
-    forest_complete_kernel(const KArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
+struct NoTop {};
+
+// The walk of every tree block of every row tile.  With TopRecords (`top`),
+// levels 0 and 1 come from the kernel parameter: the root record is warp
+// uniform, and both level-1 records are loaded (uniform) and selected, so a
+// tree's first two levels cost no shared-memory wavefront; the walk then
+// resumes at heap node 3 + 2 r0 + r1 (slot 4 + 2 r0 + r1).
+template <int KT, int G, bool PLANES, bool CAT, class Top>
+__device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* smem, const Top& top) {
+  constexpr bool kTop = !std::is_same<Top, NoTop>::value;
   const int D = a.D;
   const uint32_t NL = 1u << D;          // slots (and leaves) per tree
   auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
@@ -53,7 +61,22 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
         A[j] = fb + uint32_t(g0 + j) * NL * 8u;
         o[j] = A[j] + 8u;  // root: heap node 0 in slot 1
       }
-      for (int L = 0; L < D; ++L) {
+      if constexpr (kTop) {
+        const int t0 = 3 * (t_block + g0);
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+          const unsigned long long q0 = top.rec[t0 + 3 * j];
+          const uint32_t r0 = dev::route<PLANES, CAT>(make_uint2(unsigned(q0), unsigned(q0 >> 32)),
+                                                       rowbase, a.masks, a.data_bins);
+          const unsigned long long q1 = top.rec[t0 + 3 * j + 1];
+          const unsigned long long q2 = top.rec[t0 + 3 * j + 2];
+          const unsigned long long q = r0 ? q2 : q1;
+          const uint32_t r1 = dev::route<PLANES, CAT>(make_uint2(unsigned(q), unsigned(q >> 32)),
+                                                       rowbase, a.masks, a.data_bins);
+          o[j] = A[j] + 8u * (4u + 2u * r0 + r1);
+        }
+      }
+      for (int L = kTop ? 2 : 0; L < D; ++L) {
         uint2 r[G];
 #pragma unroll
         for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
@@ -82,6 +105,20 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
     }
   };
   dev::run_tiles<KT>(a, smem, score);
+}
+
+template <int KT, int G, bool PLANES, bool CAT>
+__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+    forest_complete_kernel(const KArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  complete_tiles<KT, G, PLANES, CAT>(a, smem, NoTop{});
+}
+
+template <int KT, int G, bool PLANES, bool CAT>
+__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+    forest_complete_top_kernel(const KArgs a, const TopRecords top) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  complete_tiles<KT, G, PLANES, CAT>(a, smem, top);
 }
 
 using KernelFn = void (*)(const KArgs);
@@ -113,7 +150,48 @@ KernelFn pick(bool planes, bool cat, int K, int G) {
   }
 }
 
+using TopKernelFn = void (*)(const KArgs, const TopRecords);
+
+template <int KT, int G>
+TopKernelFn pick3_top(bool planes, bool cat) {
+  if (planes)
+    return cat ? forest_complete_top_kernel<KT, G, true, true>
+               : forest_complete_top_kernel<KT, G, true, false>;
+  return cat ? forest_complete_top_kernel<KT, G, false, true>
+             : forest_complete_top_kernel<KT, G, false, false>;
+}
+
+// The same (K, G) pairs as pick.
+TopKernelFn pick_top(bool planes, bool cat, int K, int G) {
+  switch (K) {
+    case 1: return G == 16 ? pick3_top<1, 16>(planes, cat) : pick3_top<1, 8>(planes, cat);
+    case 2: return pick3_top<2, 8>(planes, cat);
+    case 3: return pick3_top<3, 6>(planes, cat);
+    case 4: return pick3_top<4, 8>(planes, cat);
+    case 5: return pick3_top<5, 5>(planes, cat);
+    case 6: return pick3_top<6, 6>(planes, cat);
+    case 7: return pick3_top<7, 7>(planes, cat);
+    case 8: return pick3_top<8, 8>(planes, cat);
+    case 10: return pick3_top<10, 10>(planes, cat);
+    case 12: return pick3_top<12, 12>(planes, cat);
+    case 16: return pick3_top<16, 16>(planes, cat);
+    default: return pick3_top<0, 8>(planes, cat);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_complete_top(bool planes, bool cat, const KArgs& a, const TopRecords& top,
+                                size_t smem, int grid, cudaStream_t stream, int* occupancy_out) {
+  TopKernelFn fn = pick_top(planes, cat, a.K, a.G);
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  if (occupancy_out)
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occupancy_out, fn, a.R, smem);
+  fn<<<grid, a.R, smem, stream>>>(a, top);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_complete(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
                             cudaStream_t stream, int* occupancy_out) {

@@ -215,11 +215,13 @@ def _cudart():
     return _CUDART
 
 
-@pytest.mark.parametrize("plan", ["codes=0", "codes=0,planes=0", "codes=1", "codes=1,G=8"])
+@pytest.mark.parametrize("plan", ["codes=0", "codes=0,planes=0", "codes=1", "codes=1,G=8",
+                                  "codes=0,top=1", "codes=0,planes=0,top=1", "codes=0,top=0"])
 @pytest.mark.parametrize("cfg", ["cfg1", "cfg2", "cfg3", "cfg4"])
 def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
     """Each kernel family (fp32 tiles with NaN planes, fp32 with default-left
-    flags, binned codes), forced through MACBOOST_PLAN, against the oracle."""
+    flags, binned codes; the first two levels from shared memory or from the
+    kernel parameter), forced through MACBOOST_PLAN, against the oracle."""
     core = gpu
     if cfg == "cfg4" and "G=8" in plan:
         pytest.skip("10 classes walk 10 trees per group")
@@ -231,6 +233,10 @@ def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
     assert desc["codes"] == ("codes=1" in plan)
     if "planes=0" in plan:
         assert desc["nan_planes"] is False
+    if "top=1" in plan and desc["layout"] == "complete":
+        assert desc["top_params"] is True
+    if "top=0" in plan:
+        assert desc["top_params"] is False
     om = O.model_from_dict(json.loads(text))
     X = synth.make_data(cfg, rows=5003, row_start=999, layout="row")
     raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
