@@ -43,6 +43,13 @@ __device__ __forceinline__ float lds_f32(uint32_t a) {
   asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ float4 lds_v4f(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
 __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
@@ -151,9 +158,10 @@ __device__ __forceinline__ void issue_block(const KArgs& a, int b, uint32_t dst,
 
 // Routing decision: 1 = right child.  PLANES: numeric records address the
 // slot of their default direction and compare unordered; otherwise bit0 of
-// the record selects the ordered compare for default-left.  CAT: categorical
-// records (bit1) test the node's mask at the value's code.
-template <bool PLANES, bool CAT>
+// the record selects the ordered compare for default-left, unless NONAN (a
+// tile without NaN) makes both compares equal.  CAT: categorical records
+// (bit1) test the node's mask at the value's code.
+template <bool PLANES, bool CAT, bool NONAN = false>
 __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsigned* masks,
                                           int data_bins) {
   const uint32_t addr = rowbase + ((PLANES && !CAT) ? r.x : (r.x & kRecSlotMask));
@@ -172,7 +180,9 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
     return left ^ 1u;
   }
   const float t = __uint_as_float(r.y);
-  if (PLANES) return uint32_t(!(v <= t));
+  // NONAN: the row tile holds no NaN, so the default direction cannot matter
+  // and v > t == !(v <= t) (thresholds and leaf values are never NaN)
+  if (PLANES || NONAN) return uint32_t(!(v <= t));
   return (r.x & kRecDefaultLeft) ? uint32_t(v > t) : uint32_t(!(v <= t));
 }
 
@@ -261,7 +271,7 @@ __device__ __forceinline__ void epilogue(const KArgs& a, const Acc<KT>& acc, lon
 // or streamed through two buffers), the -Inf plane fill, and the bounded-wait
 // abort protocol.  `score(fb, b, row, rowbase, acc)` walks every tree of the
 // forest block at shared address fb for this thread's row.
-template <int KT, class ScoreBlock>
+template <int KT, bool CHECK_NAN = false, class ScoreBlock>
 __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, ScoreBlock score) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -317,6 +327,19 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
     const long long row = tile * a.R + tid;
     const uint32_t rowbase = tl + uint32_t(tid) * 4u;
     fill_left_planes(a, rowbase);  // own row only: no barrier needed
+    // CHECK_NAN: the CTA scans the staged tile (16-byte loads) once; a tile
+    // without NaN lets the walk drop the default-direction test.  Rows past
+    // the end of the input hold stale values, which can only clear `clean`.
+    bool clean = false;
+    if (CHECK_NAN) {
+      const uint32_t n4 = uint32_t(a.S_stage) * uint32_t(a.R) / 4u;
+      bool nan = false;
+      for (uint32_t i = uint32_t(tid); i < n4; i += blockDim.x) {
+        const float4 q = lds_v4f(tl + 16u * i);
+        nan = nan || isnan(q.x) || isnan(q.y) || isnan(q.z) || isnan(q.w);
+      }
+      clean = !__syncthreads_or(nan);
+    }
     Acc<KT> acc;
     acc.init(a.base, a.K);
     for (int b = 0; b < a.nblocks; ++b) {
@@ -345,7 +368,7 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
         }
         fb = fbuf;
       }
-      score(fb, b, row, rowbase, acc);
+      score(fb, b, row, rowbase, acc, clean);
     }
     if (row < a.rows) epilogue<KT>(a, acc, row);
     __syncthreads();  // every thread is done with tile buffer tb

@@ -51,9 +51,12 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
   constexpr bool kTop = !std::is_same<Top, NoTop>::value;
   const int D = a.D;
   const uint32_t NL = 1u << D;          // slots (and leaves) per tree
-  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
+  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc,
+                   bool clean) {
     const int t_block = b * a.Tb;
     const uint32_t leaves = fb + a.leaf_off;
+    auto walk = [&](auto nonan_tag) {
+    constexpr bool NN = decltype(nonan_tag)::value;
     for (int g0 = 0; g0 < a.Tb; g0 += G) {
       uint32_t A[G], o[G];
 #pragma unroll
@@ -66,12 +69,12 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
 #pragma unroll
         for (int j = 0; j < G; ++j) {
           const unsigned long long q0 = top.rec[t0 + 3 * j];
-          const uint32_t r0 = dev::route<PLANES, CAT>(make_uint2(unsigned(q0), unsigned(q0 >> 32)),
+          const uint32_t r0 = dev::route<PLANES, CAT, NN>(make_uint2(unsigned(q0), unsigned(q0 >> 32)),
                                                        rowbase, a.masks, a.data_bins);
           const unsigned long long q1 = top.rec[t0 + 3 * j + 1];
           const unsigned long long q2 = top.rec[t0 + 3 * j + 2];
           const unsigned long long q = r0 ? q2 : q1;
-          const uint32_t r1 = dev::route<PLANES, CAT>(make_uint2(unsigned(q), unsigned(q >> 32)),
+          const uint32_t r1 = dev::route<PLANES, CAT, NN>(make_uint2(unsigned(q), unsigned(q >> 32)),
                                                        rowbase, a.masks, a.data_bins);
           o[j] = A[j] + 8u * (4u + 2u * r0 + r1);
         }
@@ -82,7 +85,7 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
         for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
 #pragma unroll
         for (int j = 0; j < G; ++j) {
-          const uint32_t right = dev::route<PLANES, CAT>(r[j], rowbase, a.masks, a.data_bins);
+          const uint32_t right = dev::route<PLANES, CAT, NN>(r[j], rowbase, a.masks, a.data_bins);
           o[j] = 2u * o[j] - A[j] + (right << 3);
         }
       }
@@ -103,8 +106,13 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
         }
       }
     }
+    };
+    if (!PLANES && clean)
+      walk(std::true_type{});
+    else
+      walk(std::false_type{});
   };
-  dev::run_tiles<KT>(a, smem, score);
+  dev::run_tiles<KT, !PLANES>(a, smem, score);
 }
 
 template <int KT, int G, bool PLANES, bool CAT>

@@ -5,6 +5,8 @@
 // distance to its first child, children are adjacent, and leaf records loop on
 // themselves, so the G trees of a group all take the group's step count (its
 // deepest leaf) without per-step branches and end on their leaves.
+#include <type_traits>
+
 #include "kernels_common.cuh"
 
 namespace mb {
@@ -14,7 +16,8 @@ template <int KT, int G, bool CAT>
 __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
     forest_explicit_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc) {
+  auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc,
+                   bool clean) {
     // block header: [0] trees, [1] first tree index, [4 + i] first record of
     // tree i, [4 + trees + g] steps of group g
     const int ntrees = int(dev::lds_u32(fb));
@@ -27,19 +30,28 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
       uint32_t o[G];
 #pragma unroll
       for (int j = 0; j < G; ++j) o[j] = recs + 8u * dev::lds_u32(fb + 16u + 4u * uint32_t(g0 + j));
-      for (int it = 0; it < steps; ++it) {
-        uint2 r[G];
+      auto walk = [&](auto nonan_tag) {
+        constexpr bool NN = decltype(nonan_tag)::value;
+        for (int it = 0; it < steps; ++it) {
+          uint2 r[G];
 #pragma unroll
-        for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
+          for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
 #pragma unroll
-        for (int j = 0; j < G; ++j) {
-          // records carry the child distance above the slot offset, so the
-          // slot is always masked; leaves read the -Inf slot with the
-          // default-left bit (go_right = 0) and have distance 0: they stay put
-          const uint32_t right = dev::route<false, CAT>(r[j], rowbase, a.masks, a.data_bins);
-          o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
+          for (int j = 0; j < G; ++j) {
+            // records carry the child distance above the slot offset, so the
+            // slot is always masked; leaves read the -Inf slot with the
+            // default-left bit (go_right = 0; with NN, !(-Inf <= leaf) = 0)
+            // and have distance 0: they stay put
+            const uint32_t right =
+                dev::route<false, CAT, NN>(r[j], rowbase, a.masks, a.data_bins);
+            o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
+          }
         }
-      }
+      };
+      if (clean)
+        walk(std::true_type{});
+      else
+        walk(std::false_type{});
 #pragma unroll
       for (int j = 0; j < G; ++j) acc.add(j, t_block + g0 + j, dev::lds_f32(o[j] + 4u));
       if (a.out_leaf != nullptr && row < a.rows) {
@@ -53,7 +65,7 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
       }
     }
   };
-  dev::run_tiles<KT>(a, smem, score);
+  dev::run_tiles<KT, true>(a, smem, score);
 }
 
 using KernelFn = void (*)(const KArgs);

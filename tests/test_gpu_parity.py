@@ -255,3 +255,25 @@ def test_cli_transform_kind(gpu, oracle_built, name):
         ref = O.predict_cli(m, g["raw"])
     got = core.predict_ex(h, g["X"], kind=core.KIND_CLI)
     assert_ulp(got, ref, ULP, f"{name} cli transform")
+
+
+@pytest.mark.parametrize("cfg,plan", [("cfg1", "codes=0,planes=0"), ("cfg2", "codes=0,planes=0"),
+                                      ("cfg5", "")])
+def test_nan_free_tiles(gpu, oracle_built, cfg, plan, monkeypatch):
+    """Row tiles without NaN take the walk without default-direction tests;
+    tiles with NaN keep them.  Rows with NaN in a few places, so that both kinds
+    of tile occur in one call, against the oracle."""
+    core = gpu
+    if plan:
+        monkeypatch.setenv("MACBOOST_PLAN", plan)
+    trees = {"cfg5": 60}.get(cfg)
+    text = synth.model_to_json(synth.make_model(cfg, trees=trees))
+    h = core.load_json(text)
+    om = O.model_from_dict(json.loads(text))
+    X = synth.make_data(cfg, rows=9001, row_start=31, layout="row")
+    X = np.where(np.isnan(X), np.float32(0.5), X).astype(np.float32)
+    X[4000:4003, 7] = np.nan                   # one or two tiles with NaN
+    X[8999, 2] = np.nan                        # and the last, partial tile
+    raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"{cfg} raw")
+    assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"{cfg} leaf"
