@@ -163,7 +163,10 @@ class _Handle:
 
     def __del__(self):
         if getattr(self, "ptr", None):
-            _lib.macboost_free(self.ptr)
+            try:
+                _lib.macboost_free(self.ptr)
+            except (AttributeError, TypeError):
+                pass  # interpreter shutdown: module globals already cleared
             self.ptr = None
 
 
@@ -543,7 +546,10 @@ class Dataset:
 
     def __del__(self):
         if getattr(self, "ptr", None):
-            _lib.macboost_dataset_free(self.ptr)
+            try:
+                _lib.macboost_dataset_free(self.ptr)
+            except (AttributeError, TypeError):
+                pass  # interpreter shutdown: module globals already cleared
             self.ptr = None
 
 
