@@ -58,6 +58,12 @@ class _BaseBooster:
         """Heap index of the leaf reached in every tree, (rows, n_trees) int32."""
         return self._run(X, _core.KIND_LEAF)
 
+    def predict_contrib(self, X):
+        """SHAP contributions (MacBoost's predict_contrib, __init__.py:338-348):
+        rows x (n_features + 1) per class, the expected value last; each row
+        (per class) sums to the raw prediction.  Computed on the GPU."""
+        return _core.predict_contrib_ex(self._need(), X, layout="row", devices=self.devices)
+
     def feature_importance(self, importance_type="gain"):
         return _core.feature_importance(self._need(), importance_type)
 

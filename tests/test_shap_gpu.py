@@ -175,3 +175,18 @@ def test_contrib_device_entry_point(gpu, oracle_built):
             cu.free(dx)
             cu.free(dout)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"layout {layout}"
+
+
+def test_estimator_predict_contrib(gpu, oracle_built, tmp_path):
+    """MacBoostRegressor.predict_contrib equals the reference-signature call."""
+    core = gpu
+    from macboost_b200 import MacBoostRegressor
+    text, om = covered("cfg1", 20)
+    p = tmp_path / "m.json"
+    p.write_text(text)
+    m = MacBoostRegressor.load_model(p, devices=[0])
+    X = synth.make_data("cfg1", rows=500, row_start=3, layout="row")
+    got = m.predict_contrib(X)
+    want = core.predict_contrib(core.load(p), X)
+    assert got.shape == (500, om.num_features + 1)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
