@@ -203,6 +203,29 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml" if self.nvml else "nvidia-smi"}
 
 
+def bind_near_gpu(device: int) -> str | None:
+    """Restrict this rank's threads to the CPU cores NVML reports as closest to
+    `device`, so that page-locked host buffers allocated afterwards land in that
+    socket's memory (first touch) and the host-device copies stay off the
+    inter-socket link.  Used for N > 1; returns the core list, or None."""
+    try:
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+        ncpu = os.cpu_count() or 1
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return f"{min(cpus)}-{max(cpus)} ({len(cpus)} cores)"
+    except Exception:
+        return None
+
+
 def traffic_lookup(cfg: str):
     """DRAM bytes per row measured by ncu for `cfg` (profiles/traffic_per_row.txt)."""
     p = ROOT / "profiles" / "traffic_per_row.txt"
@@ -331,6 +354,7 @@ def main():
 
     dev = dist.local_rank
     torch.cuda.set_device(dev)
+    affinity = bind_near_gpu(dev) if dist.world > 1 else None
     if args.rows:
         rows = args.rows
     elif args.scaling == "weak":
@@ -429,6 +453,8 @@ def main():
         "clocks": clk,
         "layout": desc,
     }
+    if affinity:
+        line["host_affinity"] = affinity
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, text, cfg.rows)
     if dist.rank == 0:
