@@ -190,3 +190,39 @@ def test_estimator_predict_contrib(gpu, oracle_built, tmp_path):
     want = core.predict_contrib(core.load(p), X)
     assert got.shape == (500, om.num_features + 1)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_contrib_random_models(gpu, oracle_built, seed):
+    """Random models of the predict fuzz test (categorical masks, NaN, +-Inf,
+    root-is-leaf trees, 1-5 classes) with covers from routed rows."""
+    core = gpu
+    from test_fuzz_gpu import random_model, random_rows
+    model, rng = random_model(5000 + seed)
+    synth.add_covers(model, random_rows(rng, model, 2000))
+    text = synth.model_to_json(model)
+    om = O.model_from_dict(json.loads(text))
+    X = random_rows(rng, model, 700)
+    got = core.predict_contrib_ex(core.load_json(text), X)
+    assert_contrib_close(got, O.predict_contrib(om, X), f"seed {seed}")
+
+
+def test_contrib_deep_paths_generic_kernel(gpu, oracle_built):
+    """Leaf-wise trees deeper than 12 (paths through more than 12 distinct
+    features) run the kernel's generic run-time-U path."""
+    core = gpu
+    rng = np.random.default_rng(77)
+    F = 40
+    tl = [synth._leafwise_tree(rng, 200, 16, F, synth.EDGES_256, 0.1) for _ in range(12)]
+    m = {"version": 1, "objective": 0, "numBins": 256, "baseScore": 0.0, "numFeatures": F,
+         "categorical": [], "trees": tl, "numClasses": 1, "baseScores": [0.0]}
+    Xs = rng.random((4000, F)).astype(np.float32)
+    synth.add_covers(m, Xs)
+    text = synth.model_to_json(m)
+    om = O.model_from_dict(json.loads(text))
+    depth = max(int(np.log2(len(t["feature"]) + 1)) - 1 for t in tl)
+    assert depth == 16
+    X = rng.random((900, F)).astype(np.float32)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    got = core.predict_contrib_ex(core.load_json(text), X)
+    assert_contrib_close(got, O.predict_contrib(om, X), "deep")
