@@ -326,6 +326,43 @@ int64_t macboost_dataset_num_feature_names(void *dataset); /* -1 when the file h
 const char *macboost_dataset_feature_name(void *dataset, int64_t i);
 void macboost_dataset_free(void *dataset);
 
+/* Bin a feature matrix into a dataset handle on `device`.  Replaces
+ * MacBooster.makeDataset, Sources/MacBoost/Booster.swift:392-434: the same
+ * checks and messages in the same order (numBins in 4...256 as
+ * MacBooster(params:), Booster.swift:263-265; shapes; finite labels;
+ * categorical ids, Booster.swift:1810-1826, features in ascending order),
+ * the same quantile edges (Binner.computeEdges, Sources/MacBoost/
+ * Binner.swift:25-60: every max(1, rows / 200000)-th non-NaN value, sorted,
+ * edge k = sample[min(m - 1, (k + 1) * m / (num_bins - 1))]; zeros for
+ * categorical and all-NaN features) and macboost_bin_data for the bins.  x
+ * is feature-major x[f * rows + i] and labels[rows], host memory;
+ * categorical lists n_categorical feature indices; feature_names holds cols
+ * strings, or NULL for a dataset without names.  Returns a handle
+ * (macboost_dataset_free) or NULL. */
+void *macboost_dataset_make(const float *x, int64_t rows, int64_t cols, const float *labels,
+                            int32_t num_bins, const int64_t *categorical, int64_t n_categorical,
+                            const char *const *feature_names, int32_t device, char **err);
+
+/* Write a dataset to `path` in MacBoost's .mbds format.  Replaces
+ * BinnedDataset.save, Sources/MacBoost/Dataset.swift:26-39 (byte for byte:
+ * little-endian header, sorted categorical indices, feature names as
+ * JSONEncoder's compact array, then edges, labels and bins with u64
+ * counts). */
+int32_t macboost_dataset_save(void *dataset, const char *path, char **err);
+
+/* `macboost dataset`: runDataset, Sources/MacBoostCLI/main.swift:134-154.
+ * Reads `data_path` (`format` as macboost_table_read), takes the column
+ * named `label` (NULL: "label") as labels and every other column as a
+ * feature, marks the comma-separated feature names in `categorical` (NULL:
+ * none), bins with num_bins on `device` and writes `output_path`; stores the
+ * row and feature counts.  Errors use the reference's messages ("label
+ * column 'y' not found; columns: a, b", "categorical column 'c' not found
+ * among features", the reader's and makeDataset's). */
+int32_t macboost_cli_dataset(const char *data_path, int32_t format, const char *label,
+                             const char *categorical, int32_t num_bins, int32_t device,
+                             const char *output_path, int64_t *rows_out, int64_t *cols_out,
+                             char **err);
+
 /* A model's output of `kind` (MACBOOST_KIND_*) on every row of a binned
  * dataset, rows sharded over devices[0..ndev) (ndev == 0: MACBOOST_DEVICES,
  * else the current device); `out` as macboost_predict_ex.  Each numeric

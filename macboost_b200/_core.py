@@ -89,6 +89,12 @@ def _configure(lib):
         "macboost_dataset_feature_name": (ctypes.c_char_p, [P, I64]),
         "macboost_dataset_free": (None, [P]),
         "macboost_predict_dataset": (I32, [P, P, I32, _i32_p, I32, P, _c_char_pp]),
+        "macboost_dataset_make": (P, [P, I64, I64, P, I32, ctypes.POINTER(I64), I64,
+                                      ctypes.POINTER(ctypes.c_char_p), I32, _c_char_pp]),
+        "macboost_dataset_save": (I32, [P, ctypes.c_char_p, _c_char_pp]),
+        "macboost_cli_dataset": (I32, [ctypes.c_char_p, I32, ctypes.c_char_p, ctypes.c_char_p,
+                                       I32, I32, ctypes.c_char_p, ctypes.POINTER(I64),
+                                       ctypes.POINTER(I64), _c_char_pp]),
         "macboost_num_feature_names": (I64, [P]),
         "macboost_feature_name": (ctypes.c_char_p, [P, I64]),
         "macboost_table_read": (P, [ctypes.c_char_p, I32, _c_char_pp]),
@@ -448,6 +454,20 @@ def cli_predict(handle: _Handle, data_path, output_path, fmt: str = "csv", raw: 
     return rows.value
 
 
+def cli_dataset(data_path, output_path, label: str | None = None, categorical: str | None = None,
+                num_bins: int = 256, fmt: str = "auto", device: int = 0) -> tuple[int, int]:
+    """`macboost dataset`: bin a table into a .mbds file; returns (rows, features)."""
+    rows, cols = ctypes.c_int64(0), ctypes.c_int64(0)
+    err = ctypes.c_char_p()
+    if _lib.macboost_cli_dataset(str(data_path).encode(), _format_code(fmt),
+                                 label.encode() if label is not None else None,
+                                 categorical.encode() if categorical is not None else None,
+                                 int(num_bins), int(device), str(output_path).encode(),
+                                 ctypes.byref(rows), ctypes.byref(cols), ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
+    return rows.value, cols.value
+
+
 # ---- binned data (the trainer's tiled bin layout) -------------------------
 
 def bin_data(X, edges, num_bins: int, categorical=(), layout: str = "row",
@@ -501,13 +521,16 @@ def predict_tree_binned(bins, rows: int, cols: int, num_bins: int, tree_off, fea
 
 
 class Dataset:
-    """A MacBoost binned dataset (.mbds) held by the library."""
+    """A MacBoost binned dataset (.mbds) held by the library: loaded from a
+    file (`Dataset(path)`) or binned from a matrix (`Dataset.make`)."""
 
-    def __init__(self, path):
-        err = ctypes.c_char_p()
-        self.ptr = _lib.macboost_dataset_load(str(path).encode(), ctypes.byref(err))
-        if not self.ptr:
-            raise MacBoostError(_take_error(err))
+    def __init__(self, path=None, _ptr=None):
+        if _ptr is None:
+            err = ctypes.c_char_p()
+            _ptr = _lib.macboost_dataset_load(str(path).encode(), ctypes.byref(err))
+            if not _ptr:
+                raise MacBoostError(_take_error(err))
+        self.ptr = _ptr
         self.rows = _lib.macboost_dataset_rows(self.ptr)
         self.cols = _lib.macboost_dataset_cols(self.ptr)
         self.num_bins = _lib.macboost_dataset_num_bins(self.ptr)
@@ -543,6 +566,39 @@ class Dataset:
         if n < 0:
             return None
         return [_lib.macboost_dataset_feature_name(self.ptr, i).decode() for i in range(n)]
+
+    @classmethod
+    def make(cls, X, labels, num_bins: int = 256, categorical=(), feature_names=None,
+             layout: str = "row", device: int = 0) -> "Dataset":
+        """MacBooster.makeDataset: quantile edges, validation and GPU binning."""
+        a = np.asarray(X, dtype=np.float32)
+        if a.ndim != 2:
+            raise ValueError("X must be 2-D")
+        fm = np.ascontiguousarray(a.T if layout == "row" else a)
+        cols, rows = fm.shape
+        y = np.ascontiguousarray(np.asarray(labels, dtype=np.float32).reshape(-1))
+        if y.shape[0] != rows:
+            raise ValueError(f"labels hold {y.shape[0]} values for {rows} rows")
+        cats = list(categorical)
+        carr = (ctypes.c_int64 * max(1, len(cats)))(*cats)
+        names = None
+        if feature_names is not None:
+            if len(feature_names) != cols:
+                raise ValueError(f"{len(feature_names)} feature names for {cols} features")
+            names = (ctypes.c_char_p * cols)(*[str(n).encode() for n in feature_names])
+        err = ctypes.c_char_p()
+        ptr = _lib.macboost_dataset_make(fm.ctypes.data, rows, cols, y.ctypes.data,
+                                         int(num_bins), carr, len(cats), names, int(device),
+                                         ctypes.byref(err))
+        if not ptr:
+            raise MacBoostError(_take_error(err))
+        return cls(_ptr=ptr)
+
+    def save(self, path) -> None:
+        """BinnedDataset.save: the .mbds bytes the reference writes."""
+        err = ctypes.c_char_p()
+        if _lib.macboost_dataset_save(self.ptr, str(path).encode(), ctypes.byref(err)) != 0:
+            raise MacBoostError(_take_error(err))
 
     def __del__(self):
         if getattr(self, "ptr", None):

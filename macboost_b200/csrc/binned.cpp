@@ -10,6 +10,7 @@
 #include "engine.h"
 #include "kernels.h"
 #include "model.h"
+#include "table.h"
 
 namespace mb {
 
@@ -604,6 +605,241 @@ int predict_dataset(Engine& e, const Dataset& d, int kind, const std::vector<int
       return -1;
     }
   return 0;
+}
+
+// ---- making and saving datasets --------------------------------------------
+
+namespace {
+
+std::string swift_float(float v) {
+  char b[40];
+  return std::string(b, format_float(v, b));
+}
+
+}  // namespace
+
+void compute_edges(const float* x, int64_t rows, int64_t cols, int num_bins,
+                   const std::vector<char>& categorical, std::vector<float>& edges) {
+  const int data_bins = num_bins - 1;
+  const int ne = data_bins - 1;
+  const int64_t step = std::max<int64_t>(1, rows / 200000);
+  edges.assign(size_t(cols) * size_t(ne), 0.0f);
+  auto one = [&](int64_t f) {
+    if (categorical[size_t(f)]) return;
+    std::vector<float> sample;
+    sample.reserve(size_t(rows / step + 1));
+    for (int64_t i = 0; i < rows; i += step) {
+      const float v = x[size_t(f) * size_t(rows) + size_t(i)];
+      if (!std::isnan(v)) sample.push_back(v);
+    }
+    if (sample.empty()) return;  // all-NaN column
+    std::stable_sort(sample.begin(), sample.end());
+    const int64_t m = int64_t(sample.size());
+    for (int k = 0; k < ne; ++k)
+      edges[size_t(f) * size_t(ne) + size_t(k)] =
+          sample[size_t(std::min(m - 1, (int64_t(k) + 1) * m / data_bins))];
+  };
+  const int nt = int(std::max<int64_t>(1, std::min<int64_t>(cols, std::thread::hardware_concurrency())));
+  std::vector<std::thread> th;
+  for (int t = 0; t < nt; ++t)
+    th.emplace_back([&, t] {
+      for (int64_t f = t; f < cols; f += nt) one(f);
+    });
+  for (auto& x_ : th) x_.join();
+}
+
+int make_dataset(int device, const float* x, int64_t rows, int64_t cols, const float* labels,
+                 int num_bins, const std::vector<int64_t>& categorical,
+                 const std::vector<std::string>* names, Dataset& d, std::string& err) {
+  // MacBooster(params:) (Booster.swift:263-265), then makeDataset's checks in order
+  if (num_bins < 4 || num_bins > 256) {
+    err = "Invalid input: numBins must be in 4...256, got " + std::to_string(num_bins);
+    return -1;
+  }
+  if (rows <= 0 || cols <= 0 || !x || !labels) {
+    const int64_t r = std::max<int64_t>(rows, 0), c = std::max<int64_t>(cols, 0);
+    err = "Invalid input: dataset shapes inconsistent (rows=" + std::to_string(rows) +
+          ", cols=" + std::to_string(cols) + ", X=" + std::to_string(x ? r * c : 0) +
+          ", y=" + std::to_string(labels ? r : 0) + ")";
+    return -1;
+  }
+  for (int64_t i = 0; i < rows; ++i)
+    if (!std::isfinite(labels[i])) {
+      err = "Invalid input: label at row " + std::to_string(i) + " is " +
+            swift_float(labels[i]) + "; labels must be finite";
+      return -1;
+    }
+  std::vector<int64_t> cats(categorical);
+  std::sort(cats.begin(), cats.end());
+  cats.erase(std::unique(cats.begin(), cats.end()), cats.end());
+  const int data_bins = num_bins - 1;
+  std::vector<char> is_cat(size_t(cols), 0);
+  for (int64_t f : cats) {
+    // validateCategoricals (Booster.swift:1810-1826), features in ascending order
+    if (f < 0 || f >= cols) {
+      err = "Internal error: categorical feature index " + std::to_string(f) + " out of range";
+      return -1;
+    }
+    is_cat[size_t(f)] = 1;
+    for (int64_t i = 0; i < rows; ++i) {
+      const float v = x[size_t(f) * size_t(rows) + size_t(i)];
+      if (std::isnan(v)) continue;
+      const float c = std::nearbyint(v);
+      if (!(c >= 0.0f) || c >= float(data_bins)) {
+        err = "Categorical feature " + std::to_string(f) + " has value " + swift_float(v) +
+              "; expected integer ids in 0..<" + std::to_string(data_bins) + " or NaN";
+        return -1;
+      }
+    }
+  }
+  d = Dataset();
+  d.rows = rows;
+  d.cols = cols;
+  d.num_bins = num_bins;
+  d.categorical = cats;
+  if (names) {
+    d.has_names = true;
+    d.names = *names;
+  }
+  d.labels.assign(labels, labels + rows);
+  compute_edges(x, rows, cols, num_bins, is_cat, d.edges);
+  const int64_t groups = (cols + 7) / 8;
+  d.bins.assign(size_t(groups) * 8 * size_t(rows), 0);
+  std::vector<uint8_t> flags(is_cat.begin(), is_cat.end());
+  return bin_data_host(device, x, rows, cols, 0, d.edges.data(), num_bins, flags.data(),
+                       d.bins.data(), err);
+}
+
+bool save_mbds(const Dataset& d, const char* path, std::string& err) {
+  std::string out;
+  auto put32 = [&](uint32_t v) { out.append(reinterpret_cast<const char*>(&v), 4); };
+  auto put64 = [&](uint64_t v) { out.append(reinterpret_cast<const char*>(&v), 8); };
+  put32(0x4D424453u);
+  put32(1);
+  put32(8);
+  put64(uint64_t(d.rows));
+  put32(uint32_t(d.cols));
+  put32(uint32_t(d.num_bins));
+  put32(uint32_t(d.categorical.size()));
+  for (int64_t c : d.categorical) put32(uint32_t(c));
+  // feature names as Foundation's JSONEncoder writes a [String]: compact, with
+  // '"', '\\' and '/' escaped and control characters as \b \f \n \r \t or \u00xx
+  std::string names;
+  if (d.has_names) {
+    names = "[";
+    for (size_t i = 0; i < d.names.size(); ++i) {
+      if (i) names += ',';
+      names += '"';
+      for (unsigned char ch : d.names[i]) {
+        switch (ch) {
+          case '"': names += "\\\""; break;
+          case '\\': names += "\\\\"; break;
+          case '/': names += "\\/"; break;
+          case '\b': names += "\\b"; break;
+          case '\f': names += "\\f"; break;
+          case '\n': names += "\\n"; break;
+          case '\r': names += "\\r"; break;
+          case '\t': names += "\\t"; break;
+          default:
+            if (ch < 0x20) {
+              char u[8];
+              std::snprintf(u, sizeof(u), "\\u%04x", ch);
+              names += u;
+            } else {
+              names += char(ch);
+            }
+        }
+      }
+      names += '"';
+    }
+    names += "]";
+  }
+  put32(uint32_t(names.size()));
+  out += names;
+  put64(d.edges.size());
+  out.append(reinterpret_cast<const char*>(d.edges.data()), d.edges.size() * 4);
+  put64(d.labels.size());
+  out.append(reinterpret_cast<const char*>(d.labels.data()), d.labels.size() * 4);
+  put64(d.bins.size());
+  out.append(reinterpret_cast<const char*>(d.bins.data()), d.bins.size());
+  FILE* f = std::fopen(path, "wb");
+  if (!f) {
+    err = std::string("cannot write '") + path + "'";
+    return false;
+  }
+  const bool ok = std::fwrite(out.data(), 1, out.size(), f) == out.size();
+  if (std::fclose(f) != 0 || !ok) {
+    err = std::string("error writing '") + path + "'";
+    return false;
+  }
+  return true;
+}
+
+bool cli_dataset(const char* data_path, int format, const char* label, const char* categorical,
+                 int num_bins, int device, const char* output_path, int64_t* rows_out,
+                 int64_t* cols_out, std::string& err) {
+  Table t;
+  if (!read_table(data_path, format, ColumnChooser(), false, t, err)) return false;
+  // prepare (main.swift:112-132)
+  const std::string lname = label ? label : "label";
+  int64_t lcol = -1;
+  for (size_t c = 0; c < t.header.size(); ++c)
+    if (t.header[c] == lname) {
+      lcol = int64_t(c);
+      break;
+    }
+  if (lcol < 0) {
+    std::string cols;
+    for (size_t c = 0; c < t.header.size(); ++c) cols += (c ? ", " : "") + t.header[c];
+    err = "label column '" + lname + "' not found; columns: " + cols;
+    return false;
+  }
+  const int64_t C = t.width();
+  std::vector<int64_t> fcols;
+  std::vector<std::string> names;
+  for (int64_t c = 0; c < C; ++c)
+    if (c != lcol) {
+      fcols.push_back(c);
+      names.push_back(t.header[size_t(c)]);
+    }
+  std::vector<int64_t> cats;
+  if (categorical) {
+    const std::string list(categorical);
+    size_t s = 0;
+    while (s <= list.size()) {
+      const size_t e = list.find(',', s);
+      const std::string name = list.substr(s, e == std::string::npos ? std::string::npos : e - s);
+      if (!name.empty()) {
+        const auto it = std::find(names.begin(), names.end(), name);
+        if (it == names.end()) {
+          err = "categorical column '" + name + "' not found among features";
+          return false;
+        }
+        cats.push_back(int64_t(it - names.begin()));
+      }
+      if (e == std::string::npos) break;
+      s = e + 1;
+    }
+  }
+  const int64_t rows = t.rows, F = int64_t(fcols.size());
+  std::vector<float> X, y(static_cast<size_t>(rows));
+  try {
+    X.resize(size_t(rows) * size_t(F));
+  } catch (...) {
+    err = "out of host memory";
+    return false;
+  }
+  for (int64_t i = 0; i < rows; ++i) {
+    const float* row = t.data + i * C;
+    for (int64_t j = 0; j < F; ++j) X[size_t(j) * size_t(rows) + size_t(i)] = row[fcols[size_t(j)]];
+    y[size_t(i)] = row[lcol];
+  }
+  Dataset d;
+  if (make_dataset(device, X.data(), rows, F, y.data(), num_bins, cats, &names, d, err)) return false;
+  if (!save_mbds(d, output_path, err)) return false;
+  if (rows_out) *rows_out = rows;
+  if (cols_out) *cols_out = F;
+  return true;
 }
 
 }  // namespace mb

@@ -78,6 +78,30 @@ int tree_binned_device(int device, const uint8_t* bins, int64_t rows, int64_t co
                        const float* leaf, int max_depth, int K, float* preds, int32_t* leaf_idx,
                        unsigned* status, cudaStream_t stream, std::string& err);
 
+// Binner.computeEdges (Sources/MacBoost/Binner.swift:26-55): per numeric
+// feature of feature-major x, a strided sample (step max(1, rows / 200000))
+// without NaN, sorted (stably, as Swift's sort), and the values at indices
+// min(m - 1, (k + 1) m / (numBins - 1)) for k < numBins - 2; categorical and
+// all-NaN features keep zero edges.
+void compute_edges(const float* x, int64_t rows, int64_t cols, int num_bins,
+                   const std::vector<char>& categorical, std::vector<float>& edges);
+
+// MacBooster.makeDataset (Booster.swift:392-440): validates labels (finite)
+// and categorical ids (integers in 0..<numBins-1 or NaN), computes edges,
+// bins on `device`.  x is feature-major host memory.
+int make_dataset(int device, const float* x, int64_t rows, int64_t cols, const float* labels,
+                 int num_bins, const std::vector<int64_t>& categorical,
+                 const std::vector<std::string>* names, Dataset& d, std::string& err);
+
+// BinnedDataset.save (Dataset.swift:26-39).
+bool save_mbds(const Dataset& d, const char* path, std::string& err);
+
+// runDataset (Sources/MacBoostCLI/main.swift:134-154): read a table, split
+// off the label column, bin the features, write `output_path`.
+bool cli_dataset(const char* data_path, int format, const char* label, const char* categorical,
+                 int num_bins, int device, const char* output_path, int64_t* rows_out,
+                 int64_t* cols_out, std::string& err);
+
 // A model's output of `kind` on every row of a dataset (rows sharded over
 // `devices`), row-major like engine_predict_host.
 int predict_dataset(Engine& e, const Dataset& d, int kind, const std::vector<int>& devices,

@@ -518,6 +518,62 @@ const char* macboost_dataset_feature_name(void* ds, int64_t i) {
 }
 void macboost_dataset_free(void* ds) { delete dataset(ds); }
 
+void* macboost_dataset_make(const float* x, int64_t rows, int64_t cols, const float* labels,
+                            int32_t num_bins, const int64_t* categorical, int64_t n_categorical,
+                            const char* const* feature_names, int32_t device, char** err) {
+  if (n_categorical < 0 || (n_categorical > 0 && !categorical)) {
+    set_error(err, "null argument");
+    return nullptr;
+  }
+  std::vector<int64_t> cats(categorical, categorical + n_categorical);
+  std::vector<std::string> names;
+  if (feature_names)
+    for (int64_t f = 0; f < cols; ++f) names.emplace_back(feature_names[f] ? feature_names[f] : "");
+  auto* d = new (std::nothrow) mb::Dataset();
+  if (!d) {
+    set_error(err, "out of host memory");
+    return nullptr;
+  }
+  std::string e;
+  if (mb::make_dataset(device, x, rows, cols, labels, num_bins, cats,
+                       feature_names ? &names : nullptr, *d, e)) {
+    delete d;
+    set_error(err, e);
+    return nullptr;
+  }
+  return d;
+}
+
+int32_t macboost_dataset_save(void* ds, const char* path, char** err) {
+  if (!ds || !path) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (!mb::save_mbds(*dataset(ds), path, e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
+int32_t macboost_cli_dataset(const char* data_path, int32_t format, const char* label,
+                             const char* categorical, int32_t num_bins, int32_t device,
+                             const char* output_path, int64_t* rows_out, int64_t* cols_out,
+                             char** err) {
+  if (!data_path || !output_path) {
+    set_error(err, "null argument");
+    return -1;
+  }
+  std::string e;
+  if (!mb::cli_dataset(data_path, format, label, categorical, num_bins, device, output_path,
+                       rows_out, cols_out, e)) {
+    set_error(err, e);
+    return -1;
+  }
+  return 0;
+}
+
 int32_t macboost_predict_dataset(void* handle, void* ds, int32_t kind, const int32_t* devices,
                                  int32_t ndev, void* out, char** err) {
   if (!handle || !ds || (ndev > 0 && !devices) || ndev < 0) {

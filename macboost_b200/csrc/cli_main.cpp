@@ -1,12 +1,15 @@
 // `macboost` command line front end of the B200 inference engine.
 //
-// Mirrors the inference commands of MacBoost's CLI (Sources/MacBoostCLI/
-// main.swift): `predict` (runPredict, :317-371), `importance` (:378-397),
-// `version` and `help`, with the same flag syntax (parseFlags, :82-96), the
+// Mirrors the inference-side commands of MacBoost's CLI (Sources/MacBoostCLI/
+// main.swift): `predict` (runPredict, :317-371), `dataset` (runDataset,
+// :134-154), `importance` (:378-397), `version` and `help`, with the same flag syntax (parseFlags, :82-96), the
 // same output files and messages, and exit status 1 with "error: ..." on
 // stderr for every failure.  It uses only the C ABI of libmacboostc.so.
 #include <algorithm>
+#include <chrono>
+#include <climits>
 #include <cstdio>
+#include <cerrno>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -22,6 +25,7 @@ const char* kUsage =
     "\n"
     "USAGE:\n"
     "  macboost predict --model <model.json> --data <test.csv> [options]\n"
+    "  macboost dataset --data <train.csv> --output <train.mbds> [options]\n"
     "  macboost importance --model <model.json>\n"
     "  macboost version\n"
     "\n"
@@ -36,9 +40,19 @@ const char* kUsage =
     "  --devices <list>   GPUs to shard rows over, e.g. 0,1,2,3\n"
     "                     [default: MACBOOST_DEVICES, else the current GPU]\n"
     "\n"
+    "DATASET OPTIONS (a binned .mbds file, as MacBoost's trainer reads it):\n"
+    "  --data <path>      training table                                 [required]\n"
+    "  --output <path>    .mbds file to write                            [required]\n"
+    "  --label <name>     label column name                        [default: label]\n"
+    "  --bins <n>         histogram bins incl. missing bin (4-256)   [default: 256]\n"
+    "  --categorical <cols>  comma-separated categorical column names\n"
+    "  --format <f>       csv | tsv | libsvm | auto              [default: auto]\n"
+    "  --device <n>       GPU that bins the values\n"
+    "                     [default: first of MACBOOST_DEVICES, else 0]\n"
+    "\n"
     "Empty fields and non-numeric tokens (NA, nan, ...) are missing values and\n"
-    "follow each split's learned default direction.  Training (`train`,\n"
-    "`dataset`) is not part of this inference engine.\n";
+    "follow each split's learned default direction.  Training (`train`) is not\n"
+    "part of this inference engine.\n";
 
 [[noreturn]] void fail(const std::string& message) {
   std::fprintf(stderr, "error: %s\n", message.c_str());
@@ -92,6 +106,25 @@ std::vector<int32_t> parse_devices(const std::string& s) {
   return d;
 }
 
+// --format values of loadTable (main.swift:98-110).
+int32_t parse_format(const std::string& f) {
+  if (f == "csv" || f == "tsv") return MACBOOST_FORMAT_CSV;
+  if (f == "libsvm") return MACBOOST_FORMAT_LIBSVM;
+  if (f == "auto") return MACBOOST_FORMAT_AUTO;
+  fail("unknown --format '" + f + "' (auto | csv | tsv | libsvm)");
+}
+
+// Swift's Int(String): optional sign, then decimal digits only, in range.
+bool parse_swift_int(const std::string& s, long long* v) {
+  size_t i = (!s.empty() && (s[0] == '+' || s[0] == '-')) ? 1 : 0;
+  if (i == s.size()) return false;
+  for (size_t j = i; j < s.size(); ++j)
+    if (s[j] < '0' || s[j] > '9') return false;
+  errno = 0;
+  *v = std::strtoll(s.c_str(), nullptr, 10);
+  return errno == 0;
+}
+
 int run_predict(const std::map<std::string, std::string>& flags) {
   auto get = [&](const char* k) -> const std::string* {
     auto it = flags.find(k);
@@ -103,16 +136,7 @@ int run_predict(const std::map<std::string, std::string>& flags) {
   if (!data) fail("--data is required");
   const std::string output = get("output") ? *get("output") : "predictions.csv";
   int32_t format = MACBOOST_FORMAT_CSV;
-  if (const std::string* f = get("format")) {
-    if (*f == "csv" || *f == "tsv")
-      format = MACBOOST_FORMAT_CSV;
-    else if (*f == "libsvm")
-      format = MACBOOST_FORMAT_LIBSVM;
-    else if (*f == "auto")
-      format = MACBOOST_FORMAT_AUTO;
-    else
-      fail("unknown --format '" + *f + "' (auto | csv | tsv | libsvm)");
-  }
+  if (const std::string* f = get("format")) format = parse_format(*f);
   std::vector<int32_t> devices;
   if (const std::string* d = get("devices")) devices = parse_devices(*d);
   void* h = load_model(*model);
@@ -127,6 +151,52 @@ int run_predict(const std::map<std::string, std::string>& flags) {
   }
   macboost_free(h);
   std::printf("wrote %lld predictions to %s\n", static_cast<long long>(rows), output.c_str());
+  return 0;
+}
+
+// `macboost dataset` (runDataset, main.swift:134-154).
+int run_dataset(const std::map<std::string, std::string>& flags) {
+  auto get = [&](const char* k) -> const std::string* {
+    auto it = flags.find(k);
+    return it == flags.end() ? nullptr : &it->second;
+  };
+  const std::string* data = get("data");
+  if (!data) fail("--data is required");
+  const std::string* output = get("output");
+  if (!output) fail("--output is required (e.g. train.mbds)");
+  long long bins = 256;
+  if (const std::string* b = get("bins"))
+    if (!parse_swift_int(*b, &bins)) bins = 256;
+  const int32_t format = get("format") ? parse_format(*get("format")) : MACBOOST_FORMAT_AUTO;
+  int32_t device = 0;
+  if (const std::string* d = get("device")) {
+    const std::vector<int32_t> v = parse_devices(*d);
+    if (v.size() != 1) fail("--device expects one GPU index");
+    device = v[0];
+  } else if (const char* env = std::getenv("MACBOOST_DEVICES")) {
+    const std::vector<int32_t> v = parse_devices(env);
+    if (!v.empty()) device = v[0];
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  // out-of-range counts reach the library as an out-of-range int32; the
+  // message then names the value given
+  const int32_t nb = int32_t(std::clamp<long long>(bins, INT_MIN, INT_MAX));
+  char* e = nullptr;
+  int64_t rows = 0, cols = 0;
+  if (macboost_cli_dataset(data->c_str(), format, get("label") ? get("label")->c_str() : nullptr,
+                           get("categorical") ? get("categorical")->c_str() : nullptr, nb,
+                           device, output->c_str(), &rows, &cols, &e) != 0) {
+    std::string msg = take_error(e);
+    const std::string clamped = "got " + std::to_string(nb);
+    if (nb != bins && msg.size() >= clamped.size() &&
+        msg.compare(msg.size() - clamped.size(), clamped.size(), clamped) == 0)
+      msg = msg.substr(0, msg.size() - clamped.size()) + "got " + std::to_string(bins);
+    fail(msg);
+  }
+  const double secs =
+      std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  std::printf("binned %lld rows x %lld features into %s in %.2fs\n", static_cast<long long>(rows),
+              static_cast<long long>(cols), output->c_str(), secs);
   return 0;
 }
 
@@ -174,8 +244,8 @@ int main(int argc, char** argv) {
   const std::string cmd = argc > 1 ? argv[1] : "";
   if (cmd == "predict") return run_predict(parse_flags(argc, argv, 2));
   if (cmd == "importance") return run_importance(parse_flags(argc, argv, 2));
-  if (cmd == "train" || cmd == "dataset")
-    fail("`macboost " + cmd + "` is not supported by this inference engine");
+  if (cmd == "dataset") return run_dataset(parse_flags(argc, argv, 2));
+  if (cmd == "train") fail("`macboost train` is not supported by this inference engine");
   if (cmd == "--version" || cmd == "version") {
     std::printf("macboost 1.0.0\n");
     return 0;

@@ -349,11 +349,48 @@ def predict_binned(bins: np.ndarray, rows: int, num_bins: int, sf: SplitForest, 
     return leaf
 
 
+def compute_edges(X, num_bins: int, categorical=(), layout: str = "row",
+                  sample_cap: int = 200_000) -> np.ndarray:
+    """Binner.computeEdges (Sources/MacBoost/Binner.swift:25-60): per numeric
+    feature every max(1, rows // sample_cap)-th value, NaNs dropped, sorted;
+    edge k (k < num_bins - 2) = sample[min(m - 1, (k + 1) * m // (num_bins - 1))].
+    Categorical and all-NaN features keep zeros.  cols x (num_bins - 2) fp32."""
+    a = np.asarray(X, dtype=np.float32)
+    fm = a.T if layout == "row" else a
+    cols, rows = fm.shape
+    data_bins = num_bins - 1
+    ne = data_bins - 1
+    step = max(1, rows // sample_cap)
+    edges = np.zeros((cols, ne), np.float32)
+    cats = set(int(c) for c in categorical)
+    k = np.arange(ne, dtype=np.int64)
+    for f in range(cols):
+        if f in cats:
+            continue
+        s = fm[f, ::step]
+        s = s[~np.isnan(s)]
+        m = s.size
+        if m == 0:
+            continue
+        s = np.sort(s, kind="stable")
+        edges[f] = s[np.minimum(m - 1, (k + 1) * m // data_bins)]
+    return edges.reshape(-1)
+
+
+def make_dataset(X, labels, num_bins: int, categorical=(), layout: str = "row"):
+    """MacBooster.makeDataset (Sources/MacBoost/Booster.swift:392-434) without
+    its error checks: (edges, tiled bins)."""
+    edges = compute_edges(X, num_bins, categorical, layout)
+    return edges, bin_data(X, edges, num_bins, categorical, layout)
+
+
 def write_mbds(path, bins, rows: int, cols: int, num_bins: int, categorical, feature_names,
                edges, labels) -> None:
     """A .mbds file as BinnedDataset.save writes it (Sources/MacBoost/Dataset.swift:26-39)."""
     import struct
-    names = json.dumps(feature_names, separators=(",", ":")).encode() if feature_names else b""
+    # JSONEncoder: compact, UTF-8 as is, "/" escaped
+    names = (json.dumps(list(feature_names), separators=(",", ":"), ensure_ascii=False)
+             .replace("/", "\\/").encode() if feature_names is not None else b"")
     with open(path, "wb") as fh:
         fh.write(struct.pack("<III", 0x4D424453, 1, 8))
         fh.write(struct.pack("<QII", rows, cols, num_bins))

@@ -19,24 +19,6 @@ from macboost_b200 import synth
 NUM_BINS = 64
 
 
-def quantile_edges(X, num_bins, categorical=()):
-    """cols x (num_bins - 2) upper edges as Binner.computeEdges picks them
-    (Sources/MacBoost/Binner.swift:26-55: sorted non-NaN sample, index
-    min(m - 1, (k + 1) * m / dataBins))."""
-    rows, cols = X.shape
-    data_bins = num_bins - 1
-    ne = data_bins - 1
-    E = np.zeros((cols, ne), np.float32)
-    for f in range(cols):
-        if f in categorical:
-            continue
-        s = np.sort(X[:, f][~np.isnan(X[:, f])])
-        if s.size:
-            m = s.size
-            E[f] = s[np.minimum(m - 1, ((np.arange(ne) + 1) * m) // data_bins)]
-    return E
-
-
 def binned_model(seed=0, F=20, trees=30, depth=5, K=1, cats=(18, 19), num_bins=NUM_BINS):
     """A model whose numeric thresholds are the dataset's bin edges, plus the
     rows and edges of that dataset."""
@@ -45,7 +27,7 @@ def binned_model(seed=0, F=20, trees=30, depth=5, K=1, cats=(18, 19), num_bins=N
     for c in cats:
         X[:, c] = rng.integers(0, min(32, num_bins - 1), len(X))
     X[rng.random(X.shape) < 0.07] = np.nan
-    E = quantile_edges(X, num_bins, cats)
+    E = O.compute_edges(X, num_bins, cats).reshape(F, num_bins - 2)
     thr = [E[f] for f in range(F)]
     tl = [synth._complete_tree(rng, depth, F, thr, 0.1, frozenset(cats), with_mask=True)
           for _ in range(trees * K)]
