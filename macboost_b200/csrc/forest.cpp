@@ -28,7 +28,7 @@ std::vector<int> group_options(int K) {
   }
 }
 
-int max_threads_for_group(int G) { return G >= 12 ? 256 : (G >= 10 ? 512 : 640); }
+int max_threads_for_group(int G) { return G >= 12 ? 256 : (G >= 10 ? 512 : 768); }
 
 namespace {
 
@@ -252,7 +252,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
     std::vector<size_t> node_prefix;
     double cost = 1e300;
   } best;
-  const int Rs[] = {640, 512, 384, 256, 128, 64, 32};
+  const int Rs[] = {768, 640, 512, 384, 256, 128, 64, 32};
   const PlanOverride ov;
   if (ov.codes == 1) {
     err = "binned codes requested but not applicable";
@@ -362,10 +362,15 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
                   ? (double(blocks.size()) * 1500.0 + double(p.buf_bytes) * p.nblocks / 64.0) /
                         double(R)
                   : 0.0;
-          // a single tile buffer also exposes the bulk-copy latency of each tile
+          // A resident forest runs the per-warp pipeline: a warp waiting for
+          // its next chunk leaves the SM to the other warps, so with enough
+          // warps (16 or more) one buffer hides the copies too (B200: cfg1 and
+          // cfg3 at 4 and 8 warps ran 1.7-3x slower than streamed 16-warp
+          // tiles).  Otherwise a single tile buffer exposes the bulk-copy
+          // latency of each tile.
+          const bool hidden = bufs == 2 || (p.nblocks == 1 && R >= 512);
           const double cost =
-              (bufs == 2 ? std::max(compute, load) : compute + load + 2500.0 / double(R)) +
-              stream;
+              (hidden ? std::max(compute, load) : compute + load + 2500.0 / double(R)) + stream;
           p.est_clk_per_row = cost;
           if (cost < best.cost * 0.999) {
             best.p = p;
@@ -459,11 +464,14 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
     // Heap nodes 0, 1, 2 (slots 1, 2, 3) of every tree for the kernel
     // parameter.  It removes the first two levels' shared-memory record loads,
     // which pays where those loads bound the walk: with NaN planes (one compare
-    // per node).  Without planes the walk is bound by ALU issue (flag test and
-    // compare select per node) and the constant-bank reads and selects only add
-    // to it (B200: cfg2 2.4% faster with, cfg1/cfg3 4.5% slower).
+    // per node), and with a resident forest, whose per-warp pipeline keeps the
+    // shared-memory pipe busy (B200, cfg2 without planes: 4% faster).  With
+    // streamed blocks and no planes the walk is bound by ALU issue (flag test
+    // and compare select per node) and the constant-bank reads and selects only
+    // add to it (B200: cfg1/cfg3 4.5% slower).
     const PlanOverride ov;
-    if (D >= 2 && f.Tpad <= kTopTrees && ov.top != 0 && (f.plan.planes || ov.top == 1)) {
+    if (D >= 2 && f.Tpad <= kTopTrees && ov.top != 0 &&
+        (f.plan.planes || f.plan.nblocks == 1 || ov.top == 1)) {
       f.top_recs.resize(size_t(f.Tpad) * 3);
       for (int t = 0; t < f.Tpad; ++t) {
         const int b = t / Tb, i = t % Tb;

@@ -78,7 +78,7 @@ constexpr uint32_t kMaxChildDelta = 16383u;
 
 // Shared-memory budget per CTA on B200 (sm_100: 227 KB opt-in).
 constexpr size_t kSmemBudget = 232448;
-constexpr size_t kSmemHeader = 128;  // mbarriers
+constexpr size_t kSmemHeader = 640;  // mbarriers: 4 per CTA at 0, then 2 per warp at 128
 
 // Deepest forest flattened to the complete layout.
 constexpr int kMaxCompleteDepth = 8;

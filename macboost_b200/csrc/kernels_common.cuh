@@ -18,7 +18,7 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 // need the larger per-thread register budget (mb::max_threads_for_group).
 template <int G>
 struct Bounds {
-  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 ? 512 : 640);
+  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 ? 512 : 768);
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -378,6 +378,144 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
       issue_tile(a, next, tiles, bar_tile0, lane);
     }
   }
+}
+
+// The per-warp pipeline, for a forest resident in shared memory (one block):
+// each warp stages and scores its own chunks of 32 rows, independently of the
+// other warps of the CTA.  Chunk c covers rows [32c, 32c + 32); warp w of CTA
+// b takes chunks (b * W + w) + k * gridDim.x * W, so the chunks in flight at
+// any time form one contiguous run of rows.  A chunk lands, one bulk copy of
+// 128 bytes per staged slot, in the warp's 32 columns of the row-tile layout
+// (slot s, row j of the warp at tile + 4 * (s * R + 32 w + j)), on the warp's
+// own mbarrier.  With two tile buffers the next chunk is in flight while the
+// current one is scored; with one, the next copy is issued when the warp is
+// done, and the other warps keep the SM busy meanwhile.  No CTA-wide barrier
+// follows the forest wait, and a chunk's NaN test is a warp vote.
+template <int KT, bool CHECK_NAN = false, class ScoreBlock>
+__device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, ScoreBlock score) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int W = int(blockDim.x >> 5);
+  const uint32_t base = smem_u32(smem);
+  const uint32_t bar_f0 = base + 16;
+  const uint32_t bar_w = base + 128u + 16u * uint32_t(warp);  // buffers 0 and 1
+  const uint32_t tiles = base + uint32_t(kSmemHeader);
+  const uint32_t fbuf = tiles + uint32_t(a.tile_bufs) * a.tile_bytes;
+  const bool bulk = a.bulk && a.S_stage > 0;
+  const long long nchunks = (a.rows + 31) / 32;
+  const long long stride = (long long)gridDim.x * W;
+  long long c = (long long)blockIdx.x * W + warp;
+
+  if (tid == 0) {
+    mbar_init(bar_f0, 1);
+    fence_mbar_init();
+  }
+  if (lane == 0) {
+    mbar_init(bar_w, 1);
+    mbar_init(bar_w + 8u, 1);
+    fence_mbar_init();
+  }
+  if (a.neg_inf_slot != 0xFFFFFFFFu) {
+    for (int b = 0; b < a.tile_bufs; ++b)
+      sts_f32(tiles + uint32_t(b) * a.tile_bytes + a.neg_inf_slot + uint32_t(tid) * 4u,
+              -__int_as_float(0x7f800000));
+  }
+  __syncthreads();
+  if (c >= nchunks) return;  // warp 0 has the CTA's first chunk: nothing was issued
+  if (warp == 0) issue_block(a, 0, fbuf, bar_f0, lane);
+
+  auto issue = [&](long long cc, int buf) {
+    const long long r0 = cc * 32;
+    long long nv = a.rows - r0;
+    if (nv > 32) nv = 32;
+    const uint32_t nbytes = uint32_t(((nv + 3) & ~3ll) * 4);
+    const uint32_t bar = bar_w + 8u * uint32_t(buf);
+    if (lane == 0) mbar_arrive_expect_tx(bar, nbytes * uint32_t(a.S_stage));
+    __syncwarp();
+    const uint32_t dst = tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u;
+    for (int s = lane; s < a.S_stage; s += 32) {
+      const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
+      bulk_g2s(dst + uint32_t(s) * uint32_t(a.R) * 4u, a.x + f * a.ld + r0, nbytes, bar);
+    }
+  };
+  // Before a copy overwrites a buffer this warp has read or written.
+  auto release = [&]() {
+    __syncwarp();
+    fence_proxy_async();
+    __syncwarp();
+  };
+
+  if (bulk) issue(c, 0);
+  bool forest_ready = false;
+  for (int k = 0; c < nchunks; c += stride, ++k) {
+    const int buf = (a.tile_bufs == 2) ? (k & 1) : 0;
+    const long long cn = c + stride;
+    const bool ahead = bulk && a.tile_bufs == 2 && cn < nchunks;
+    if (ahead) {
+      release();  // buffer buf^1 held chunk k-1
+      issue(cn, buf ^ 1);
+    }
+    const uint32_t rowbase = tiles + uint32_t(buf) * a.tile_bytes + uint32_t(tid) * 4u;
+    const long long row = c * 32 + lane;
+    if (bulk) {
+      const uint32_t parity = (a.tile_bufs == 2) ? uint32_t((k >> 1) & 1) : uint32_t(k & 1);
+      const bool ok = mbar_wait(bar_w + 8u * uint32_t(buf), parity, a.err);
+      if (__any_sync(0xffffffffu, !ok)) {
+        // the copy of chunk k+1 may still be in flight: let it land (bounded)
+        if (ahead) mbar_wait(bar_w + 8u * uint32_t(buf ^ 1), uint32_t(((k + 1) >> 1) & 1), a.err);
+        return;
+      }
+    } else {
+      for (int s = 0; s < a.S_stage; ++s) {
+        const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
+        sts_f32(rowbase + uint32_t(s) * uint32_t(a.R) * 4u,
+                row < a.rows ? __ldg(a.x + f * a.ld + row) : 0.0f);
+      }
+      __syncwarp();
+    }
+    if (!forest_ready) {
+      const bool ok = mbar_wait(bar_f0, 0, a.err);
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (ahead) mbar_wait(bar_w + 8u * uint32_t(buf ^ 1), uint32_t(((k + 1) >> 1) & 1), a.err);
+        return;
+      }
+      forest_ready = true;
+    }
+    fill_left_planes(a, rowbase);  // own row only
+    // CHECK_NAN: the warp scans its 32 rows of every staged slot (16-byte
+    // loads, 8 lanes per slot); rows past the end of the input hold stale
+    // values, which can only clear `clean`.
+    bool clean = false;
+    if (CHECK_NAN) {
+      const uint32_t slice = tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u;
+      bool nan = false;
+      for (int i = lane; i < a.S_stage * 8; i += 32) {
+        const float4 q = lds_v4f(slice + uint32_t(i >> 3) * uint32_t(a.R) * 4u +
+                                 uint32_t(i & 7) * 16u);
+        nan = nan || isnan(q.x) || isnan(q.y) || isnan(q.z) || isnan(q.w);
+      }
+      clean = !__any_sync(0xffffffffu, nan);
+    }
+    Acc<KT> acc;
+    acc.init(a.base, a.K);
+    score(fbuf, 0, row, rowbase, acc, clean);
+    if (row < a.rows) epilogue<KT>(a, acc, row);
+    if (bulk && a.tile_bufs == 1 && cn < nchunks) {
+      release();
+      issue(cn, 0);
+    }
+  }
+}
+
+// The pipeline for the forest block layout: per-warp chunks when the forest
+// is resident, else CTA-wide tiles with streamed tree blocks.
+template <int KT, bool CHECK_NAN = false, class ScoreBlock>
+__device__ __forceinline__ void run_rows(const KArgs& a, unsigned char* smem, ScoreBlock score) {
+  if (a.nblocks == 1)
+    run_warps<KT, CHECK_NAN>(a, smem, score);
+  else
+    run_tiles<KT, CHECK_NAN>(a, smem, score);
 }
 
 }  // namespace dev

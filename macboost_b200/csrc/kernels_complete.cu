@@ -11,10 +11,12 @@
 //
 // Execution model.  One persistent CTA per SM, one thread per row of a row
 // tile of R rows.  The tile's feature columns come from HBM by cp.async.bulk
-// (one copy of R consecutive fp32 values per staged feature, completing on an
-// mbarrier); with two tile buffers the next tile streams in while the current
-// one is scored.  The forest -- or, when larger than shared memory, one block
-// of trees at a time through two buffers -- is staged the same way.  Each
+// completing on mbarriers.  With the forest resident in shared memory each
+// warp stages and scores its own 32-row chunks (one 128-byte copy per staged
+// feature, the warp's own mbarrier), so a warp waiting for its rows leaves the
+// SM to the others; a forest larger than shared memory streams one block of
+// trees at a time through two buffers, with CTA-wide tiles of R rows (one copy
+// of R values per staged feature, one or two tile buffers).  Each
 // thread walks G trees at once (G independent chains of shared-memory loads)
 // and adds their leaves to fp32 accumulators strictly in tree order.
 //
@@ -112,7 +114,7 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
     else
       walk(std::false_type{});
   };
-  dev::run_tiles<KT, !PLANES>(a, smem, score);
+  dev::run_rows<KT, !PLANES>(a, smem, score);
 }
 
 template <int KT, int G, bool PLANES, bool CAT>

@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
       }
     }
   };
-  dev::run_tiles<KT, true>(a, smem, score);
+  dev::run_rows<KT, true>(a, smem, score);
 }
 
 using KernelFn = void (*)(const KArgs);
