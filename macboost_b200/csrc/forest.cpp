@@ -28,7 +28,14 @@ std::vector<int> group_options(int K) {
   }
 }
 
-int max_threads_for_group(int G) { return G >= 12 ? 256 : (G >= 10 ? 512 : 768); }
+int max_threads_for_group(int K, int G) {
+  // must match dev::Bounds (kernels_common.cuh); K outside the dedicated
+  // instantiations runs the generic kernel (KT = 0)
+  const bool dedicated = K >= 1 && K <= 8;  // else the generic kernel (KT = 0)
+  if (G >= 12) return 256;
+  if (G >= 10 || !dedicated || K >= 5) return 512;
+  return K <= 2 ? 768 : 640;
+}
 
 namespace {
 
@@ -283,7 +290,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
       // explicit layout: one more slot holding -Inf, read by leaf records
       const int S_tile = std::max(sp.S_total, 1) + (complete ? 0 : 1);
       for (int R : Rs) {
-        if (R > max_threads_for_group(G) || (ov.R && R != ov.R)) continue;
+        if (R > max_threads_for_group(m.K, G) || (ov.R && R != ov.R)) continue;
         for (int bufs = 2; bufs >= 1; --bufs) {
           if (ov.bufs && bufs != ov.bufs) continue;
           const size_t tile = round_up(size_t(S_tile) * R * 4, 128);

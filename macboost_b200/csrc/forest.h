@@ -89,9 +89,9 @@ enum class Layout : int { kComplete = 0, kExplicit = 1 };
 // Trees walked concurrently by one thread (independent dependency chains).
 // Always a multiple of K, so that tree j of a group scores class j % K.  The
 // planner picks one of group_options(K); groups of 12 or more trees need the
-// register budget of at most max_threads_for_group(G) threads per CTA.
+// register budget of at most max_threads_for_group(K, G) threads per CTA.
 std::vector<int> group_options(int K);
-int max_threads_for_group(int G);
+int max_threads_for_group(int K, int G);
 
 struct LaunchPlan {
   int R = 0;              // rows per tile == threads per CTA

@@ -47,7 +47,12 @@ struct FeatureUse {
   std::vector<float> thr;  // numeric thresholds (with repeats until sorted)
 };
 
-int max_threads_codes(int G) { return G >= 12 ? 256 : (G >= 10 ? 512 : 768); }
+// must match CodesBounds (kernels_codes.cu); K outside the dedicated
+// instantiations runs the generic kernel (KT = 0)
+int max_threads_codes(int K, int G) {
+  const bool dedicated = K >= 1 && K <= 8;
+  return G >= 12 ? 256 : (G >= 10 || !dedicated || K >= 5 ? 512 : 768);
+}
 
 }  // namespace
 
@@ -171,7 +176,7 @@ bool flatten_codes(const Model& m, FlatForest& f, std::string& why, int force_G,
     if (force_G && G != force_G) continue;
     const int ngroups = (g.T + G - 1) / G;
     for (int R : Rs) {
-      if (R > max_threads_codes(G) || (force_R && R != force_R)) continue;
+      if (R > max_threads_codes(m.K, G) || (force_R && R != force_R)) continue;
       const size_t raw = round_up(size_t(std::max(g.S_stage, 1)) * R * 4, 128);
       const size_t codes = round_up(size_t(code_words) * R * 4, 128);
       // record offsets must fit 18 bits

@@ -27,9 +27,9 @@ constexpr uint32_t kCodeCatBit = 0x2000u;
 constexpr uint32_t kCodeIndexMask = 0x1FFFu;
 constexpr int kCodeOffsetShift = 14;
 
-template <int G>
+template <int KT, int G>
 struct CodesBounds {
-  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 ? 512 : 768);
+  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 || KT == 0 || KT >= 5 ? 512 : 768);
 };
 
 template <int CW>
@@ -124,7 +124,7 @@ __device__ __forceinline__ uint32_t code_route(uint32_t r, uint32_t code_row,
 }
 
 template <int KT, int G, int CW, bool CAT>
-__global__ void __launch_bounds__(CodesBounds<G>::kMaxThreads, 1)
+__global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
     forest_codes_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x;

@@ -14,11 +14,14 @@ namespace dev {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
-// Threads per CTA the kernels are compiled for: groups of 12 or more trees
-// need the larger per-thread register budget (mb::max_threads_for_group).
-template <int G>
+// Threads per CTA the kernels are compiled for (mb::max_threads_for_group):
+// groups of 10 or more trees, and more than two classes' accumulators, need
+// the larger per-thread register budget of fewer threads.
+template <int KT, int G>
 struct Bounds {
-  static constexpr int kMaxThreads = G >= 12 ? 256 : (G >= 10 ? 512 : 768);
+  static constexpr int kMaxThreads =
+      G >= 12 ? 256
+              : (G >= 10 || KT == 0 || KT >= 5 ? 512 : ((KT == 1 || KT == 2) ? 768 : 640));
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -118,14 +118,14 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
 }
 
 template <int KT, int G, bool PLANES, bool CAT>
-__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+__global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_complete_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   complete_tiles<KT, G, PLANES, CAT>(a, smem, NoTop{});
 }
 
 template <int KT, int G, bool PLANES, bool CAT>
-__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+__global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_complete_top_kernel(const KArgs a, const TopRecords top) {
   extern __shared__ __align__(128) unsigned char smem[];
   complete_tiles<KT, G, PLANES, CAT>(a, smem, top);

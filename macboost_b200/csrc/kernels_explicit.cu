@@ -13,7 +13,7 @@ namespace mb {
 namespace {
 
 template <int KT, int G, bool CAT>
-__global__ void __launch_bounds__(dev::Bounds<G>::kMaxThreads, 1)
+__global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_explicit_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   auto score = [&](uint32_t fb, int b, long long row, uint32_t rowbase, dev::Acc<KT>& acc,
