@@ -24,8 +24,9 @@ CLI = PKG / "macboost"          # the `macboost` command (C++ over the C ABI)
 
 CXX_SOURCES = ["model.cpp", "forest.cpp", "forest_codes.cpp", "shap.cpp", "engine.cpp",
                "table.cpp", "binned.cpp", "capi.cpp"]
-CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_explicit.cu", "kernels_codes.cu",
-              "kernels_shap.cu", "kernels_binned.cu", "noalloc.cu"]
+CU_SOURCES = ["kernels.cu", "kernels_complete.cu", "kernels_complete_fixed.cu",
+              "kernels_explicit.cu", "kernels_codes.cu", "kernels_shap.cu", "kernels_binned.cu",
+              "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -277,3 +277,30 @@ def test_nan_free_tiles(gpu, oracle_built, cfg, plan, monkeypatch):
     raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
     assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"{cfg} raw")
     assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"{cfg} leaf"
+
+
+@pytest.mark.parametrize("depth", [3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("plan", ["codes=0,G=8", "codes=0,G=8,planes=0", "codes=0,G=8,top=1",
+                                  "codes=0,G=8,planes=0,top=1", "codes=0,G=8,top=0"])
+def test_fixed_depth_builds(gpu, oracle_built, depth, plan, monkeypatch):
+    """Single-class forests of depth 4-8 in 8-tree groups run the fixed-depth
+    kernel builds (depth 3: the run-time-depth build), with and without NaN
+    planes and top-level parameters, categorical splits and NaN rows (tiles
+    with and without NaN), against the oracle."""
+    core = gpu
+    monkeypatch.setenv("MACBOOST_PLAN", plan)
+    rng = np.random.default_rng(700 + depth)
+    F, cats = 30, frozenset({27, 28, 29})
+    tl = [synth._complete_tree(rng, depth, F, synth.EDGES_256, 0.1, cats, with_mask=True)
+          for _ in range(37)]
+    m = {"version": 1, "objective": 1, "numBins": 256, "baseScore": -0.2, "numFeatures": F,
+         "categorical": sorted(cats), "trees": tl, "numClasses": 1, "baseScores": [-0.2]}
+    text = synth.model_to_json(m)
+    h = core.load_json(text)
+    om = O.model_from_dict(json.loads(text))
+    X = rng.random((20_000, F), dtype=np.float32)
+    X[:, 27:] = rng.integers(-2, 260, (20_000, 3))
+    X[10_000:][rng.random((10_000, F)) < 0.05] = np.nan     # the second half holds NaN
+    raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"d{depth} {plan} raw")
+    assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"d{depth} leaf"
