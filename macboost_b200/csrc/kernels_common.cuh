@@ -186,7 +186,12 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
   // NONAN: the row tile holds no NaN, so the default direction cannot matter
   // and v > t == !(v <= t) (thresholds and leaf values are never NaN)
   if (PLANES || NONAN) return uint32_t(!(v <= t));
-  return (r.x & kRecDefaultLeft) ? uint32_t(v > t) : uint32_t(!(v <= t));
+  // NaN to the default side with one unordered compare: max(v, -Inf) turns
+  // NaN into -Inf (left of every threshold) and leaves any other value as it
+  // is; max(v, NaN) leaves every value, NaN included, as it is, and the
+  // unordered compare sends NaN right (fmax returns the non-NaN operand).
+  const float c = __uint_as_float((r.x & kRecDefaultLeft) ? 0xFF800000u : 0x7FC00000u);
+  return uint32_t(!(fmaxf(v, c) <= t));
 }
 
 // Per-thread accumulators: KT compile-time classes, or (KT == 0) up to 128.
