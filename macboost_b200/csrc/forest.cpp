@@ -349,8 +349,8 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
           // Cost model (SM clocks per row), calibrated on B200 (cfg2-like
           // depth-6 forests): a warp scores one tree in ~24 SM clocks when the
           // shared-memory pipe is saturated (~19 wavefronts: two per 8-byte
-          // record load, one per gather, two for the leaf), ~32 without NaN
-          // planes (23 on NaN-free row chunks, 36 on chunks with NaN, issue-
+          // record load, one per gather, two for the leaf), ~28 without NaN
+          // planes (23 on NaN-free row chunks, 29 on chunks with NaN, issue-
           // bound on the default-direction max and compare); saturation needs
           // warps more than per-thread tree groups: efficiency ~ (warps/16)^0.45
           // * (G/8)^0.15.  Staging uses the SM's share of HBM bandwidth
@@ -358,7 +358,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
           // add barriers and L2 traffic.
           const int Tpad = blocks.empty() ? 0 : blocks.back().first + blocks.back().second;
           const double levels = complete ? double(D) : avg_depth * 1.15;
-          const double per_tree = (planes || !any_left ? 24.0 : 32.0) * levels / 6.0 *
+          const double per_tree = (planes || !any_left ? 24.0 : 28.0) * levels / 6.0 *
                                   (complete ? 1.0 : 1.3);
           const double warps = double(R) / 32.0;
           const double eff =

@@ -190,7 +190,12 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
   // NaN into -Inf (left of every threshold) and leaves any other value as it
   // is; max(v, NaN) leaves every value, NaN included, as it is, and the
   // unordered compare sends NaN right (fmax returns the non-NaN operand).
-  const float c = __uint_as_float((r.x & kRecDefaultLeft) ? 0xFF800000u : 0x7FC00000u);
+  // c is 0x7FC00000 (NaN) shifted left by the default-left bit: 0xFF800000
+  // (-Inf).  A numeric record's low five bits are that bit (bit 0) and zeros
+  // (slot offsets are multiples of 128 bytes), and the funnel shift takes its
+  // count modulo 32, so the record word itself is the shift count.
+  static_assert(kRecDefaultLeft == 1u && (kRecSlotMask & 31u) == 0u, "record layout");
+  const float c = __uint_as_float(__funnelshift_l(0u, 0x7FC00000u, r.x));
   return uint32_t(!(fmaxf(v, c) <= t));
 }
 
