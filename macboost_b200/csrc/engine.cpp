@@ -96,6 +96,7 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.search_depth = f.search_depth;
   a.code_tile_bytes = f.code_tile_bytes;
   a.neg_inf_slot = f.neg_inf_slot_bytes;
+  a.compact_children = f.compact_children ? 1 : 0;
   a.data_bins = e.model.num_bins - 1;
   a.kind = kind;
   a.log_link = e.model.uses_log_link() ? 1 : 0;

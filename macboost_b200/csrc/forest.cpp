@@ -493,6 +493,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
   } else {
     f.leaf_heap.assign(node_prefix.back(), -1);
     f.block_rec_base.assign(size_t(nb), 0);
+    uint32_t max_delta = 0;
     // Leaf records loop on themselves: they read the constant -Inf slot (the
     // tile slot after all staged and -Inf-plane slots) with the default-left
     // flag, so go_right = (-Inf > leaf value) is 0, and their child distance is
@@ -543,12 +544,29 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
             return false;
           }
           rec.x |= delta << kRecChildShift;
+          max_delta = std::max(max_delta, delta);
           r[q] = rec;
           order.push_back(2 * o + 1);
           order.push_back(2 * o + 2);
           next += 2;
         }
         f.nodes += int64_t(order.size());
+      }
+    }
+    // With every child distance at most kMaxCompactDelta, store 8 x the
+    // distance: the walk then adds the field to the record address directly.
+    f.compact_children = max_delta <= kMaxCompactDelta;
+    if (f.compact_children) {
+      for (int b = 0; b < nb; ++b) {
+        const int t0 = blocks[size_t(b)].first, n = blocks[size_t(b)].second;
+        uint8_t* blk = f.blob.data() + f.block_off[size_t(b)];
+        const size_t rec_off = round_up(16 + 4 * size_t(n + n / Gsel), 16);
+        auto* recs = reinterpret_cast<uint2_like*>(blk + rec_off);
+        const size_t count = node_prefix[size_t(t0 + n)] - node_prefix[size_t(t0)];
+        for (size_t q = 0; q < count; ++q) {
+          const uint32_t d = recs[q].x >> kRecChildShift;
+          recs[q].x = (recs[q].x & ((1u << kRecChildShift) - 1u)) | ((d * 8u) << kRecChildShift);
+        }
       }
     }
   }
@@ -571,6 +589,8 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"nan_planes\":" + std::string(f.plan.planes ? "true" : "false");
   s += ",\"codes\":" + std::string(f.codes ? "true" : "false");
   s += ",\"top_params\":" + std::string(f.top_recs.empty() ? "false" : "true");
+  if (f.layout == Layout::kExplicit)
+    s += ",\"compact_children\":" + std::string(f.compact_children ? "true" : "false");
   if (f.codes) {
     s += ",\"code_bytes\":" + std::to_string(f.code_bytes);
     s += ",\"code_slots\":" + std::to_string(f.S_code);

@@ -75,6 +75,7 @@ constexpr uint32_t kRecFullMask = 4u;
 constexpr uint32_t kRecSlotMask = 0x3FF80u;   // bits 7..17
 constexpr int kRecChildShift = 18;
 constexpr uint32_t kMaxChildDelta = 16383u;
+constexpr uint32_t kMaxCompactDelta = 2047u;  // 8 x distance still fits bits 18-31
 
 // Shared-memory budget per CTA on B200 (sm_100: 227 KB opt-in).
 constexpr size_t kSmemBudget = 232448;
@@ -132,6 +133,9 @@ struct FlatForest {
   // forest is deeper than it allows (more than kTopTrees trees, or D < 2)
   std::vector<uint64_t> top_recs;
   uint32_t neg_inf_slot_bytes = 0xFFFFFFFFu;  // explicit: tile offset of the -Inf slot
+  // explicit: record bits 18-31 hold 8 x the child distance (every distance
+  // at most kMaxCompactDelta), else the distance itself
+  bool compact_children = false;
 
   // Binned-code layout (see forest_codes.cpp): each staged value becomes its
   // rank among the forest's distinct thresholds of that feature, stored as

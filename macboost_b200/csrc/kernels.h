@@ -46,6 +46,7 @@ struct KArgs {
   int search_depth;
   unsigned code_tile_bytes;
   unsigned neg_inf_slot;           // explicit layout: tile offset of the constant -Inf slot
+  int compact_children;            // explicit layout: record bits 18-31 hold 8 x child distance
   unsigned buf_bytes, leaf_off, tile_bytes;
   int data_bins;
   // Output.

@@ -12,7 +12,8 @@
 namespace mb {
 namespace {
 
-template <int KT, int G, bool CAT>
+// COMPACT: record bits 18-31 hold 8 x the child distance (a byte offset).
+template <int KT, int G, bool CAT, bool COMPACT>
 __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_explicit_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -44,7 +45,10 @@ __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
             // and have distance 0: they stay put
             const uint32_t right =
                 dev::route<false, CAT, NN>(r[j], rowbase, a.masks, a.data_bins);
-            o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
+            if (COMPACT)
+              o[j] += (r[j].x >> kRecChildShift) + (right ? 8u : 0u);
+            else
+              o[j] += ((r[j].x >> kRecChildShift) + right) * 8u;
           }
         }
       };
@@ -71,27 +75,31 @@ __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
 using KernelFn = void (*)(const KArgs);
 
 template <int KT, int G>
-KernelFn pick3(bool cat) {
-  return cat ? forest_explicit_kernel<KT, G, true> : forest_explicit_kernel<KT, G, false>;
+KernelFn pick3(bool cat, bool compact) {
+  if (compact)
+    return cat ? forest_explicit_kernel<KT, G, true, true>
+               : forest_explicit_kernel<KT, G, false, true>;
+  return cat ? forest_explicit_kernel<KT, G, true, false>
+             : forest_explicit_kernel<KT, G, false, false>;
 }
 
 // (K, G) pairs must match mb::group_options (forest.cpp).  NaN planes need no
 // separate instantiation: explicit records always mask the slot offset and
 // clear the default-left bit when planes are in use.
-KernelFn pick(bool, bool cat, int K, int G) {
+KernelFn pick(bool, bool cat, bool compact, int K, int G) {
   switch (K) {
-    case 1: return G == 16 ? pick3<1, 16>(cat) : pick3<1, 8>(cat);
-    case 2: return pick3<2, 8>(cat);
-    case 3: return pick3<3, 6>(cat);
-    case 4: return pick3<4, 8>(cat);
-    case 5: return pick3<5, 5>(cat);
-    case 6: return pick3<6, 6>(cat);
-    case 7: return pick3<7, 7>(cat);
-    case 8: return pick3<8, 8>(cat);
-    case 10: return pick3<10, 10>(cat);
-    case 12: return pick3<12, 12>(cat);
-    case 16: return pick3<16, 16>(cat);
-    default: return pick3<0, 8>(cat);
+    case 1: return G == 16 ? pick3<1, 16>(cat, compact) : pick3<1, 8>(cat, compact);
+    case 2: return pick3<2, 8>(cat, compact);
+    case 3: return pick3<3, 6>(cat, compact);
+    case 4: return pick3<4, 8>(cat, compact);
+    case 5: return pick3<5, 5>(cat, compact);
+    case 6: return pick3<6, 6>(cat, compact);
+    case 7: return pick3<7, 7>(cat, compact);
+    case 8: return pick3<8, 8>(cat, compact);
+    case 10: return pick3<10, 10>(cat, compact);
+    case 12: return pick3<12, 12>(cat, compact);
+    case 16: return pick3<16, 16>(cat, compact);
+    default: return pick3<0, 8>(cat, compact);
   }
 }
 
@@ -99,7 +107,7 @@ KernelFn pick(bool, bool cat, int K, int G) {
 
 cudaError_t launch_explicit(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
                             cudaStream_t stream, int* occupancy_out) {
-  KernelFn fn = pick(planes, cat, a.K, a.G);
+  KernelFn fn = pick(planes, cat, a.compact_children != 0, a.K, a.G);
   cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;

@@ -304,3 +304,28 @@ def test_fixed_depth_builds(gpu, oracle_built, depth, plan, monkeypatch):
     raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
     assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"d{depth} {plan} raw")
     assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o), f"d{depth} leaf"
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_explicit_child_encodings(gpu, oracle_built, wide):
+    """Explicit-layout records store 8 x the child distance when every
+    distance is at most 2047, else the distance itself (a complete depth-12
+    tree has distances up to 4095); both walks against the oracle."""
+    core = gpu
+    rng = np.random.default_rng(91 + wide)
+    F = 24
+    tl = [synth._leafwise_tree(rng, 120, 11, F, synth.EDGES_256, 0.1) for _ in range(15)]
+    if wide:
+        tl.insert(7, synth._complete_tree(rng, 12, F, synth.EDGES_256, 0.1))
+    m = {"version": 1, "objective": 0, "numBins": 256, "baseScore": 0.1, "numFeatures": F,
+         "categorical": [], "trees": tl, "numClasses": 1, "baseScores": [0.1]}
+    text = synth.model_to_json(m)
+    h = core.load_json(text)
+    d = json.loads(core.describe(h))
+    assert d["layout"] == "explicit" and d["compact_children"] is (not wide)
+    om = O.model_from_dict(json.loads(text))
+    X = rng.random((6000, F), dtype=np.float32)
+    X[3000:][rng.random((3000, F)) < 0.1] = np.nan
+    raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)
+    assert_bitwise(core.predict_ex(h, X, kind=core.KIND_RAW), raw_o, f"wide={wide}")
+    assert np.array_equal(core.predict_ex(h, X, kind=core.KIND_LEAF), leaf_o)
