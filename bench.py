@@ -398,7 +398,12 @@ def main():
     for _ in range(args.steps):
         step()
     ev1.record(stream)
-    clocks.sample()            # the queued steps are running now
+    # sample while the queued steps run (a blocking synchronize can keep the
+    # sampler thread from running); the device timing is unaffected
+    clocks.sample()
+    while not ev1.query():
+        clocks.sample()
+        time.sleep(0.001)
     torch.cuda.synchronize(dev)
     dist.barrier()
     launches = _core.kernel_launches() - launches0
@@ -480,7 +485,12 @@ def _time_steps(step, steps, warmup, stream, dist, clocks=None):
         step()
     ev1.record(stream)
     if clocks:
+        # sample while the queued launches run (a blocking synchronize can keep
+        # the sampler thread from running); the device timing is unaffected
         clocks.sample()
+        while not ev1.query():
+            clocks.sample()
+            time.sleep(0.001)
     torch.cuda.synchronize()
     dist.barrier()
     ms_local = ev0.elapsed_time(ev1)
