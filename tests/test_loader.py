@@ -175,3 +175,33 @@ def test_cols_mismatch_is_an_error(lib_built):
     h = core.load_json(_variant())
     with pytest.raises(core.MacBoostError, match="model expects 2 features, got 3"):
         core.predict(h, np.zeros((4, 3), np.float32))
+
+
+def test_plan_thread_bounds_by_class_count(lib_built):
+    """Tiles of up to 768 threads for one or two classes, 640 for three or
+    four, 512 for five to eight (their kernels' register budgets)."""
+    core = lib_built
+    rng = np.random.default_rng(3)
+    for K, cap in ((1, 768), (2, 768), (3, 640), (4, 640), (5, 512), (8, 512)):
+        tl = [synth._complete_tree(rng, 4, 6, synth.EDGES_256, 0.1) for _ in range(4 * K)]
+        m = {"version": 1, "objective": 7 if K > 2 else 1, "numBins": 256, "baseScore": 0.0,
+             "numFeatures": 6, "categorical": [], "trees": tl, "numClasses": K,
+             "baseScores": [0.0] * K}
+        d = json.loads(core.describe(core.load_json(synth.model_to_json(m))))
+        assert d["rows_per_tile"] <= cap, (K, d["rows_per_tile"])
+
+
+def test_explicit_child_encoding_choice(lib_built):
+    """Explicit records hold 8 x the child distance when every distance is at
+    most 2047; a complete depth-12 tree (distances up to 4095) keeps the plain
+    distance."""
+    core = lib_built
+    rng = np.random.default_rng(5)
+    leafwise = [synth._leafwise_tree(rng, 100, 11, 10, synth.EDGES_256, 0.1) for _ in range(3)]
+    base = {"version": 1, "objective": 0, "numBins": 256, "baseScore": 0.0, "numFeatures": 10,
+            "categorical": [], "numClasses": 1, "baseScores": [0.0]}
+    d = json.loads(core.describe(core.load_json(synth.model_to_json({**base, "trees": leafwise}))))
+    assert d["layout"] == "explicit" and d["compact_children"] is True
+    wide = leafwise + [synth._complete_tree(rng, 12, 10, synth.EDGES_256, 0.1)]
+    d = json.loads(core.describe(core.load_json(synth.model_to_json({**base, "trees": wide}))))
+    assert d["layout"] == "explicit" and d["compact_children"] is False
