@@ -364,9 +364,11 @@ namespace {
 // kernel checks features and children as it walks).
 struct DevTrees {
   DevBuf off, feature, sbin, flags, mask, leaf;
+  long long nodes = 0;
   int put(int T, const int64_t* tree_off, const int32_t* f, const uint32_t* b,
           const uint32_t* fl, const uint32_t* cm, const float* lv, std::string& err) {
     const size_t N = size_t(tree_off[T]);
+    nodes = (long long)(N - size_t(tree_off[0]));
     std::vector<long long> o(tree_off, tree_off + T + 1);
     return upload(off, o.data(), o.size(), err) || upload(feature, f, N, err) ||
                    upload(sbin, b, N, err) || upload(flags, fl, N, err) ||
@@ -391,6 +393,7 @@ BinnedArgs tree_args(const DevTrees& t, int T, int64_t rows, int64_t cols, int n
   a.leaf = t.leaf.as<float>();
   a.max_depth = max_depth;
   a.K = K;
+  a.node_hint = t.nodes;
   return a;
 }
 

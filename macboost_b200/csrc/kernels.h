@@ -144,6 +144,8 @@ struct BinnedArgs {
   const float* base;
   KArgs ka;
   unsigned* err;                // kErrBadTree when a split names a missing feature or child
+  long long node_hint;          // nodes of all T trees when the caller knows them, else 0
+  unsigned rec_cap;             // set by launch_binned: shared bytes for staged node records
 };
 constexpr unsigned kErrBadTree = 2u;
 cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream);

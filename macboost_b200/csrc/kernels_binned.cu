@@ -9,6 +9,7 @@
 // 8-byte word.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "kernels.h"
@@ -123,6 +124,65 @@ __device__ __forceinline__ unsigned walk_staged(const BinnedArgs& a, int t, uint
   return node;
 }
 
+// Staged node records (one 8-byte record per node, every tree of the call,
+// copied to shared memory once per CTA): x = split bin (bits 0-7) | default
+// left (bit 8) | categorical (bit 9) | leaf (bit 10) | bad split (bit 11) |
+// byte offset of the feature's bin in a staged row (bits 15-31: tile g at
+// g * R * 8, bin f % 8 within the row's word); y = the node's global index
+// (its categorical mask).  A bad split names a feature outside the matrix or
+// a child outside its tree, checked once here instead of at every level.
+constexpr uint32_t kRecBinDL = 1u << 8, kRecBinCat = 1u << 9, kRecBinLeaf = 1u << 10,
+                   kRecBinBad = 1u << 11;
+constexpr int kRecBinOffShift = 15;
+
+__device__ __forceinline__ void stage_records(const BinnedArgs& a, uint32_t recs, int R) {
+  const long long g0 = __ldg(a.tree_off);
+  for (int t = 0; t < a.T; ++t) {
+    const long long b0 = __ldg(a.tree_off + t);
+    const long long nodes = __ldg(a.tree_off + t + 1) - b0;
+    for (long long n = threadIdx.x; n < nodes; n += blockDim.x) {
+      const long long q = b0 + n;
+      const int f = __ldg(a.feature + q);
+      uint32_t x;
+      if (f < 0) {
+        x = kRecBinLeaf;
+      } else if (f >= a.cols || 2ll * n + 2 >= nodes) {
+        x = kRecBinBad;
+      } else {
+        const unsigned fl = __ldg(a.flags + q);
+        const uint32_t off = uint32_t(f >> 3) * uint32_t(R) * 8u + uint32_t(f & 7);
+        x = (__ldg(a.sbin + q) & 0xFFu) | ((fl & 1u) ? kRecBinDL : 0u) |
+            ((fl & 2u) ? kRecBinCat : 0u) | (off << kRecBinOffShift);
+      }
+      asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(recs + uint32_t(q - g0) * 8u),
+                   "r"(x), "r"(uint32_t(q)) : "memory");
+    }
+  }
+}
+
+// The walk over staged records of one tree (records of its root at `tree`):
+// the same rule as walk_staged.
+__device__ __forceinline__ unsigned walk_records(const BinnedArgs& a, uint32_t tree,
+                                                 uint32_t row, unsigned last) {
+  unsigned node = 0;
+  for (int d = 0; d < a.max_depth; ++d) {
+    const uint2 r = dev::lds_v2(tree + node * 8u);
+    if (r.x & (kRecBinLeaf | kRecBinBad)) {
+      if (r.x & kRecBinBad) atomicOr(a.err, kErrBadTree);
+      break;
+    }
+    unsigned b;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(b) : "r"(row + (r.x >> kRecBinOffShift)));
+    bool left;
+    if (r.x & kRecBinCat)
+      left = (__ldg(a.catmask + size_t(r.y) * 8 + (b >> 5)) >> (b & 31)) & 1u;
+    else
+      left = (b == last) ? (r.x & kRecBinDL) != 0 : b <= (r.x & 0xFFu);
+    node = 2u * node + (left ? 1u : 2u);
+  }
+  return node;
+}
+
 // Persistent CTAs over row tiles of R = blockDim rows; each tile's bins (one
 // R x 8-byte run per feature tile, 16-byte aligned) arrive by cp.async.bulk,
 // double-buffered on two mbarriers with bounded waits, so the bin matrix is
@@ -146,11 +206,23 @@ __global__ void __launch_bounds__(256) binned_staged_kernel(const BinnedArgs a) 
       dev::bulk_g2s(buf0 + buf * tile_bytes + uint32_t(g) * uint32_t(R) * 8u,
                     a.bins + (size_t(g) * size_t(a.n) + size_t(r0)) * 8, bytes, bar);
   };
+  // node records after the two tile buffers, when every tree of the call fits
+  const uint32_t recs = buf0 + 2u * tile_bytes;
+  const long long total_nodes = __ldg(a.tree_off + a.T) - __ldg(a.tree_off);
+  bool staged = total_nodes >= 0 && total_nodes * 8 <= (long long)a.rec_cap;
+  if (staged) {  // uniform over the CTA: the offsets must not decrease
+    bool mono = true;
+    for (int t = tid; t < a.T; t += R)
+      mono = mono && __ldg(a.tree_off + t + 1) >= __ldg(a.tree_off + t);
+    staged = __syncthreads_and(mono);
+  }
+  const unsigned last = unsigned((a.num_bins - 1) & 0xFF);
   if (tid == 0) {
     dev::mbar_init(bar0, 1);
     dev::mbar_init(bar0 + 8, 1);
     dev::fence_mbar_init();
   }
+  if (staged && blockIdx.x < ntiles) stage_records(a, recs, R);
   __syncthreads();
   if (tid == 0 && blockIdx.x < ntiles) issue(blockIdx.x, 0);
   uint32_t parity = 0;
@@ -165,9 +237,20 @@ __global__ void __launch_bounds__(256) binned_staged_kernel(const BinnedArgs a) 
     const long long i = tile * R + tid;
     if (i < a.n) {
       const uint32_t tb = buf0 + buf * tile_bytes;
+      const uint32_t row = tb + uint32_t(tid) * 8u;
+      const long long g0 = __ldg(a.tree_off);
+      auto walk = [&](int t) -> unsigned {
+        if (!staged) return walk_staged(a, t, tb, tid, R);
+        const long long b0 = __ldg(a.tree_off + t);
+        if (__ldg(a.tree_off + t + 1) <= b0) {  // a tree without nodes
+          atomicOr(a.err, kErrBadTree);
+          return 0u;
+        }
+        return walk_records(a, recs + uint32_t(b0 - g0) * 8u, row, last);
+      };
       if (!FOREST) {
         for (int t = 0; t < a.T; ++t) {
-          const unsigned node = walk_staged(a, t, tb, tid, R);
+          const unsigned node = walk(t);
           if (a.preds)
             a.preds[size_t(t % a.K) * size_t(a.n) + i] += __ldg(a.leaf + __ldg(a.tree_off + t) + node);
           if (a.leaf_idx) a.leaf_idx[size_t(t) * size_t(a.n) + i] = int(node);
@@ -176,7 +259,7 @@ __global__ void __launch_bounds__(256) binned_staged_kernel(const BinnedArgs a) 
         dev::Acc<KT> acc;
         acc.init(a.base, a.K);
         for (int t = 0; t < a.T; ++t) {
-          const unsigned node = walk_staged(a, t, tb, tid, R);
+          const unsigned node = walk(t);
           if (a.ka.kind == kKindLeaf)
             a.ka.out_leaf[size_t(i) * a.T + t] = int(node);
           else
@@ -237,9 +320,18 @@ cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream) {
   // per feature tile must fit in shared memory
   const long long groups = (a.cols + 7) / 8;
   const int R = 256;
-  const size_t smem = 128 + 2 * size_t(groups) * R * 8;
+  const size_t tiles = 128 + 2 * size_t(groups) * R * 8;
   if ((a.n % 2) == 0 && (reinterpret_cast<uintptr_t>(a.bins) % 16) == 0 && groups > 0 &&
-      smem <= 200 * 1024) {
+      tiles <= 200 * 1024) {
+    // node records (8 bytes each) beside the tiles: room for all of the call's
+    // nodes when the caller counted them (up to 96 KB), else 8 KB, enough for
+    // one tree of up to 1,024 nodes; the kernel stages them when they fit (it
+    // reads the node count itself)
+    BinnedArgs b = a;
+    const size_t avail = std::min<size_t>(96 * 1024, 200 * 1024 - tiles);
+    const size_t rec_bytes = a.node_hint > 0 ? size_t(a.node_hint) * 8 : 8 * 1024;
+    b.rec_cap = rec_bytes <= avail ? uint32_t((rec_bytes + 15) / 16 * 16) : 0u;
+    const size_t smem = tiles + b.rec_cap;
     const long long ntiles = (a.n + R - 1) / R;
     void (*k)(const BinnedArgs) = !a.forest_mode ? binned_staged_kernel<1, false>
                                   : a.K == 1     ? binned_staged_kernel<1, true>
@@ -251,7 +343,7 @@ cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     const long long want = (long long)(per_sm < 1 ? 1 : per_sm) * sms;
     const int grid = int(ntiles < want ? ntiles : want);
-    k<<<grid, R, smem, stream>>>(a);
+    k<<<grid, R, smem, stream>>>(b);
     return cudaGetLastError();
   }
   const long long want = (a.n + 255) / 256;
