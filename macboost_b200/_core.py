@@ -76,6 +76,8 @@ def _configure(lib):
         "macboost_bin_data": (I32, [P, I64, I64, I32, P, I32, P, I32, P, _c_char_pp]),
         "macboost_predict_tree_binned": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P, I32,
                                                I32, I32, P, P, _c_char_pp]),
+        "macboost_predict_tree_binned_device": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P,
+                                                      I32, I32, I32, P, P, P, P, _c_char_pp]),
         "macboost_dataset_load": (P, [ctypes.c_char_p, _c_char_pp]),
         "macboost_dataset_rows": (I64, [P]),
         "macboost_dataset_cols": (I64, [P]),
@@ -518,6 +520,23 @@ def predict_tree_binned(bins, rows: int, cols: int, num_bins: int, tree_off, fea
             li.ctypes.data if li is not None else None, ctypes.byref(err)) != 0:
         raise MacBoostError(_take_error(err))
     return li
+
+
+def predict_tree_binned_device(bins_ptr: int, rows: int, cols: int, num_bins: int,
+                               num_trees: int, tree_off_ptr: int, feature_ptr: int,
+                               split_bin_ptr: int, flags_ptr: int, catmask_ptr: int,
+                               leaf_ptr: int, max_depth: int, num_classes: int, device: int,
+                               preds_ptr: int, leaf_idx_ptr: int, status_ptr: int,
+                               stream: int = 0) -> None:
+    """macboost_predict_tree_binned_device: every pointer is device memory; the
+    walk is enqueued on `stream` and a bad split ORs 2 into the status word."""
+    err = ctypes.c_char_p()
+    if _lib.macboost_predict_tree_binned_device(
+            bins_ptr, rows, cols, num_bins, num_trees, tree_off_ptr, feature_ptr,
+            split_bin_ptr, flags_ptr, catmask_ptr, leaf_ptr, max_depth, num_classes, device,
+            preds_ptr or None, leaf_idx_ptr or None, status_ptr, stream or None,
+            ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
 
 
 class Dataset:

@@ -103,3 +103,76 @@ def test_predict_dataset_equals_float_predict(gpu, oracle_built, tmp_path, K):
                        f"kind {kind}")
     assert np.array_equal(core.predict_dataset(h, d, core.KIND_LEAF),
                           core.predict_ex(h, X, kind=core.KIND_LEAF))
+
+
+def _split_arrays(sf):
+    return [np.ascontiguousarray(sf.tree_off, np.int64), np.ascontiguousarray(sf.feature, np.int32),
+            np.ascontiguousarray(sf.bin, np.uint32), np.ascontiguousarray(sf.flags, np.uint32),
+            np.ascontiguousarray(sf.catmask, np.uint32), np.ascontiguousarray(sf.leaf, np.float32)]
+
+
+@pytest.mark.parametrize("trees,depth", [(40, 5), (1, 10), (260, 5)])
+def test_tree_binned_record_staging_and_fallback(gpu, oracle_built, trees, depth):
+    """The walk stages a call's trees in shared memory when they fit and reads
+    the split arrays otherwise: through the host call (all nodes counted: 40
+    trees of 63 nodes staged, 260 trees, 16,380 nodes, too many) and the
+    device call (8 KB of records: one 63-node tree staged per call, a 2,047-node
+    tree too large), against the oracle, preds and leaf indices bit for bit."""
+    core = gpu
+    from test_gpu_parity import _cudart
+    m, X, E = binned_model(seed=60 + depth, trees=trees, depth=depth)
+    om = O.model_from_dict(json.loads(synth.model_to_json(m)))
+    bins = O.bin_data(X, E, NUM_BINS, m["categorical"])
+    sf = O.split_form(om, E, NUM_BINS)
+    rows, cols = X.shape
+    start = np.random.default_rng(2).standard_normal(rows).astype(np.float32)
+    want = start.copy()
+    want_leaf = O.predict_binned(bins, rows, NUM_BINS, sf, depth, 1, want, want_leaf=True)
+    got = start.copy()
+    got_leaf = core.predict_tree_binned(bins, rows, cols, NUM_BINS, sf.tree_off, sf.feature,
+                                        sf.bin, sf.flags, sf.catmask, sf.leaf, depth, 1,
+                                        preds=got, want_leaf=True)
+    assert_bitwise(got, want, "host call")
+    assert np.array_equal(got_leaf, want_leaf)
+    # the device entry point, one tree per call as a GPU trainer calls it
+    cu = _cudart()
+    T = len(sf.tree_off) - 1
+    arrs = _split_arrays(sf)
+    dbins = cu.alloc(bins.nbytes)
+    dpreds = cu.alloc(rows * 4)
+    dleaf = cu.alloc(rows * 4)
+    dstatus = cu.alloc(4)
+    dptrs = [cu.alloc(max(a.nbytes, 4)) for a in arrs]
+    try:
+        cu.h2d(dbins, np.ascontiguousarray(bins))
+        cu.h2d(dpreds, start)
+        cu.h2d(dstatus, np.zeros(1, np.uint32))
+        for d, a in zip(dptrs, arrs):
+            cu.h2d(d, a)
+        leaves = []
+        for t in range(min(T, 12)):
+            a0, a1 = int(sf.tree_off[t]), int(sf.tree_off[t + 1])
+            off = np.array([a0, a1], np.int64)
+            doff = cu.alloc(16)
+            try:
+                cu.h2d(doff, off)
+                core.predict_tree_binned_device(
+                    dbins, rows, cols, NUM_BINS, 1, doff, dptrs[1], dptrs[2], dptrs[3], dptrs[4],
+                    dptrs[5], depth, 1, 0, dpreds, dleaf, dstatus)
+                leaves.append(cu.d2h(dleaf, rows, np.int32))
+            finally:
+                cu.free(doff)
+        status = cu.d2h(dstatus, 1, np.uint32)[0]
+        preds = cu.d2h(dpreds, rows, np.float32)
+    finally:
+        for d in [dbins, dpreds, dleaf, dstatus, *dptrs]:
+            cu.free(d)
+    assert status == 0
+    n = min(T, 12)
+    part = start.copy()
+    part_leaf = O.predict_binned(bins, rows, NUM_BINS, O.SplitForest(
+        tree_off=sf.tree_off[:n + 1], feature=sf.feature, bin=sf.bin, flags=sf.flags,
+        catmask=sf.catmask, leaf=sf.leaf), depth, 1, part, want_leaf=True)
+    assert_bitwise(preds, part, "device call, tree by tree")
+    for t in range(n):
+        assert np.array_equal(leaves[t], part_leaf[t]), f"tree {t} leaves"
