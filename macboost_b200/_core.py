@@ -74,6 +74,8 @@ def _configure(lib):
         "macboost_predict_contrib_device": (I32, [P, I32, P, I64, I64, I64, I32, P, P,
                                                   _c_char_pp]),
         "macboost_bin_data": (I32, [P, I64, I64, I32, P, I32, P, I32, P, _c_char_pp]),
+        "macboost_bin_data_device": (I32, [P, I64, I64, I64, I32, P, I32, P, I32, P, P,
+                                           _c_char_pp]),
         "macboost_predict_tree_binned": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P, I32,
                                                I32, I32, P, P, _c_char_pp]),
         "macboost_predict_tree_binned_device": (I32, [P, I64, I64, I32, I32, P, P, P, P, P, P,
@@ -520,6 +522,17 @@ def predict_tree_binned(bins, rows: int, cols: int, num_bins: int, tree_off, fea
             li.ctypes.data if li is not None else None, ctypes.byref(err)) != 0:
         raise MacBoostError(_take_error(err))
     return li
+
+
+def bin_data_device(x_ptr: int, rows: int, cols: int, ld: int, layout: int, edges_ptr: int,
+                    num_bins: int, categorical_ptr: int, device: int, bins_ptr: int,
+                    stream: int = 0) -> None:
+    """macboost_bin_data_device: device pointers, enqueued on `stream`."""
+    err = ctypes.c_char_p()
+    if _lib.macboost_bin_data_device(x_ptr, rows, cols, ld, layout, edges_ptr, num_bins,
+                                     categorical_ptr, device, bins_ptr, stream or None,
+                                     ctypes.byref(err)) != 0:
+        raise MacBoostError(_take_error(err))
 
 
 def predict_tree_binned_device(bins_ptr: int, rows: int, cols: int, num_bins: int,

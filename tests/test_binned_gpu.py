@@ -176,3 +176,36 @@ def test_tree_binned_record_staging_and_fallback(gpu, oracle_built, trees, depth
     assert_bitwise(preds, part, "device call, tree by tree")
     for t in range(n):
         assert np.array_equal(leaves[t], part_leaf[t]), f"tree {t} leaves"
+
+
+def test_bin_data_device_entry_point(gpu, oracle_built):
+    """macboost_bin_data_device on device buffers (feature-major with a padded
+    stride, and row-major) equals the host call byte for byte."""
+    core = gpu
+    from test_gpu_parity import _cudart
+    cu = _cudart()
+    rng = np.random.default_rng(14)
+    rows, cols, nb, ld = 5001, 19, 64, 5008
+    X = (rng.standard_normal((rows, cols)) * 2).astype(np.float32)
+    X[:, 2] = rng.integers(-2, 70, rows)
+    X[rng.random(X.shape) < 0.05] = np.nan
+    E = np.sort(rng.standard_normal((cols, nb - 2)), axis=1).astype(np.float32)
+    cats = np.zeros(cols, np.uint8)
+    cats[2] = 1
+    want = core.bin_data(X, E, nb, [2], layout="row")
+    fm = np.zeros((cols, ld), np.float32)
+    fm[:, :rows] = X.T
+    for src, layout, stride in ((fm, core.LAYOUT_FEATURE_MAJOR, ld),
+                                (np.ascontiguousarray(X), core.LAYOUT_ROW_MAJOR, cols)):
+        bufs = [cu.alloc(src.nbytes), cu.alloc(E.nbytes), cu.alloc(cols), cu.alloc(want.nbytes)]
+        try:
+            cu.h2d(bufs[0], src)
+            cu.h2d(bufs[1], E)
+            cu.h2d(bufs[2], cats)
+            core.bin_data_device(bufs[0], rows, cols, stride, layout, bufs[1], nb, bufs[2], 0,
+                                 bufs[3])
+            got = cu.d2h(bufs[3], want.size, np.uint8)
+        finally:
+            for b in bufs:
+                cu.free(b)
+        assert np.array_equal(got, want), f"layout {layout}"
