@@ -33,7 +33,8 @@ int max_threads_for_group(int K, int G) {
   // instantiations runs the generic kernel (KT = 0)
   const bool dedicated = K >= 1 && K <= 8;  // else the generic kernel (KT = 0)
   if (G >= 12) return 256;
-  if (G >= 10 || !dedicated || K >= 5) return 512;
+  if (G >= 10) return 384;
+  if (!dedicated || K >= 5) return 512;
   return K <= 2 ? 768 : 640;
 }
 

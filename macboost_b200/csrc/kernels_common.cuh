@@ -21,7 +21,8 @@ template <int KT, int G>
 struct Bounds {
   static constexpr int kMaxThreads =
       G >= 12 ? 256
-              : (G >= 10 || KT == 0 || KT >= 5 ? 512 : ((KT == 1 || KT == 2) ? 768 : 640));
+              : (G >= 10 ? 384
+                         : (KT == 0 || KT >= 5 ? 512 : ((KT == 1 || KT == 2) ? 768 : 640)));
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
