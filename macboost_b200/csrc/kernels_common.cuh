@@ -59,6 +59,11 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ void sts_v4f(uint32_t a, float4 v) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void sts_f32(uint32_t a, float v) {
   asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
@@ -144,6 +149,25 @@ __device__ __forceinline__ void fill_left_planes(const KArgs& a, uint32_t rowbas
     const float v = lds_f32(rowbase + src);
     sts_f32(rowbase + dst, isnan(v) ? -__int_as_float(0x7f800000) : v);
   }
+}
+
+// The same for a warp's 32-row slice (slot s of the slice at slice + s * R
+// * 4): eight lanes copy one slot's 128 bytes with 16-byte accesses, four
+// slots per pass.  Lanes write other lanes' rows, so the warp syncs after.
+__device__ __forceinline__ void fill_left_planes_warp(const KArgs& a, uint32_t slice, int lane) {
+  const float ninf = -__int_as_float(0x7f800000);
+  const uint32_t part = uint32_t(lane & 7) * 16u;
+  for (int i = lane >> 3; i < a.n_conv; i += 4) {
+    const uint32_t src = uint32_t(__ldg(a.conv_src + i)) * uint32_t(a.R) * 4u;
+    const uint32_t dst = uint32_t(__ldg(a.conv_dst + i)) * uint32_t(a.R) * 4u;
+    float4 v = lds_v4f(slice + src + part);
+    v.x = isnan(v.x) ? ninf : v.x;
+    v.y = isnan(v.y) ? ninf : v.y;
+    v.z = isnan(v.z) ? ninf : v.z;
+    v.w = isnan(v.w) ? ninf : v.w;
+    sts_v4f(slice + dst + part, v);
+  }
+  __syncwarp();
 }
 
 // Warp 0: stage forest block b (16 KB bulk copies spread over the lanes).
@@ -496,7 +520,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       }
       forest_ready = true;
     }
-    fill_left_planes(a, rowbase);  // own row only
+    fill_left_planes_warp(a, tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u, lane);
     // CHECK_NAN: the warp scans its 32 rows of every staged slot (16-byte
     // loads, 8 lanes per slot); rows past the end of the input hold stale
     // values, which can only clear `clean`.
