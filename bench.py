@@ -10,13 +10,25 @@ features, 100 depth-6 trees, fused sigmoid output).  Rows shard with no
 collective on the data path; torch.distributed (gloo, CPU tensors) is used
 only for the barriers and the max-over-ranks of the timings.
 
+Scaling (the configs' own splits): cfg1-cfg4 are strong-scaled -- the
+config's rows are split into N contiguous shards; cfg5 runs proportional
+slices -- 50M / 8 rows per GPU, so N GPUs predict N/8 of the 50M rows (weak).
+
 value  -- device-resident input: K launches timed with CUDA events on the
           launching stream, max over ranks.
 e2e    -- the reference-facing C-ABI call (macboost_predict_ex) on page-locked
           host buffers: host->device copy, kernel and device->host copy of the
           outputs inside the timed region, max over ranks.
 cpu_baseline -- the oracle (C restatement of the reference CPU predictor,
-          all host threads) on a bounded row sample, rank 0, N == 1 only.
+          all host threads) on a bounded prefix of the timed rows, rank 0,
+          N == 1 only; the same leg compares those rows' GPU outputs with the
+          oracle's ("parity": raw margins bit for bit, the step's transformed
+          output within 2 ulp).  When the reference's own Python package is
+          installed in baseline/_ref, its numpy predictor (PyModel.predict_raw)
+          is timed beside it ("cpu_baseline_reference").
+e2e_copy_ceiling -- plain page-locked H2D and D2H copies of the same bytes as
+          an e2e step, timed with CUDA events while every rank copies at once
+          (max over ranks): the host-link bound of the e2e number.
 --impl reference -- times that CPU predictor as the reference arm.
 """
 
@@ -251,25 +263,81 @@ def measured_peak_hbm():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(cfg, text, rows_total, budget_s=10.0, threads=None):
-    """Oracle (C restatement of predictCPU) on a bounded row sample."""
+def cpu_baseline(cfg, text, X, budget_s=10.0, threads=None):
+    """Oracle (C restatement of predictCPU) on a bounded prefix of the timed
+    rows X (feature-major, F x rows).  Returns the baseline and the oracle's
+    raw margins of those rows (the parity check's reference)."""
     from oracle import oracle as O
     O.build()
     om = O.model_from_dict(json.loads(text))
     nt = threads or os.cpu_count() or 1
+    rows_total = X.shape[1]
     probe = min(rows_total, 20_000)
-    X = synth.make_data(cfg, rows=probe, layout="feature", seed=cfg.data_seed + 99)
     t0 = time.perf_counter()
-    O.predict_raw(om, X, layout="feature", nthreads=nt)
+    O.predict_raw(om, X[:, :probe], layout="feature", nthreads=nt)
     dt = max(time.perf_counter() - t0, 1e-6)
     n = int(min(rows_total, max(probe, probe * budget_s / dt)))
-    X = synth.make_data(cfg, rows=n, layout="feature", seed=cfg.data_seed + 99)
+    Xs = np.ascontiguousarray(X[:, :n])
     t0 = time.perf_counter()
-    O.predict_raw(om, X, layout="feature", nthreads=nt)
+    raw = O.predict_raw(om, Xs, layout="feature", nthreads=nt)
     dt = time.perf_counter() - t0
     return {"value": n * cfg.trees / dt, "unit": UNIT, "cores": nt, "kind": "port",
-            "sample": f"{n} rows of {cfg.name} x {cfg.trees} trees, {dt:.2f} s, "
-                      f"{nt} threads (oracle/mbref.c, restatement of Booster.swift predictCPU)"}
+            "sample": f"the first {n} of the timed rows of {cfg.name} x {cfg.trees} trees, "
+                      f"{dt:.2f} s, {nt} threads (oracle/mbref.c, restatement of "
+                      f"Booster.swift predictCPU)"}, raw, om
+
+
+def parity_check(O, om, raw_o, raw_gpu, out_gpu, kind):
+    """The timed step's outputs of the rows the oracle scored, against it."""
+    n = raw_o.shape[0]
+    raw_bitwise = bool(np.array_equal(np.ascontiguousarray(raw_gpu[:n]).view(np.uint32),
+                                      np.ascontiguousarray(raw_o).view(np.uint32)))
+    if kind == 2:
+        want = O.predict_proba(raw_o if om.num_classes > 1 else raw_o[:, 0]).astype(np.float32)
+    else:
+        want = raw_o
+    got = np.ascontiguousarray(out_gpu[:n], dtype=np.float32)
+    ulp = int(O.ulp_distance(got, want).max()) if n else 0
+    return {"rows": int(n), "raw_bitwise": raw_bitwise, "output_max_ulp": ulp,
+            "output_within_2_ulp": ulp <= 2,
+            "against": "oracle/mbref.c (restatement of Booster.swift predictCPU, pinned to "
+                       "the reference's PyModel outputs in tests/golden)"}
+
+
+def reference_pymodel(cfg, text, X, budget_s=10.0):
+    """The reference's own CPU predictor, PyModel.predict_raw
+    (python/macboost/_pyinfer.py:52-72), imported unmodified from the package
+    installed in baseline/_ref, timed on a bounded prefix of the timed rows;
+    None when that package is not installed on this machine."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "macboost" / "_pyinfer.py").exists():
+        return None
+    import importlib.util
+    import tempfile
+    spec = importlib.util.spec_from_file_location("_mb_ref_pyinfer",
+                                                  ref / "macboost" / "_pyinfer.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    with tempfile.NamedTemporaryFile("w", suffix=".json", delete=False) as fh:
+        fh.write(text)
+        path = fh.name
+    try:
+        pm = mod.PyModel(path)
+    finally:
+        os.unlink(path)
+    probe = min(X.shape[1], 2_000)
+    t0 = time.perf_counter()
+    pm.predict_raw(np.ascontiguousarray(X[:, :probe].T))
+    dt = max(time.perf_counter() - t0, 1e-6)
+    n = int(min(X.shape[1], max(probe, probe * budget_s / dt)))
+    Xr = np.ascontiguousarray(X[:, :n].T)
+    t0 = time.perf_counter()
+    pm.predict_raw(Xr)
+    dt = time.perf_counter() - t0
+    return {"value": n * cfg.trees / dt, "unit": UNIT, "cores": 1, "kind": "reference",
+            "sample": f"the first {n} of the timed rows x {cfg.trees} trees, {dt:.2f} s; "
+                      f"PyModel.predict_raw (numpy, one process) from the reference package "
+                      f"installed unmodified in baseline/_ref; host has {os.cpu_count()} cores"}
 
 
 def run_reference(args, dist, cfg, text):
@@ -302,10 +370,31 @@ def run_reference(args, dist, cfg, text):
                     "d2h_bytes_per_step": 0}}
 
 
+def default_scaling(cfg) -> str:
+    """cfg5 runs proportional slices (50M / 8 rows per GPU); the others split
+    the config's rows over the GPUs."""
+    return "weak" if cfg.name == "cfg5" else "strong"
+
+
+def rows_per_rank(cfg, args, world) -> int:
+    if args.rows:
+        rows = args.rows
+    elif args.scaling == "weak":
+        rows = cfg.rows // 8 if cfg.name == "cfg5" else cfg.rows
+    else:
+        rows = cfg.rows // world
+    return (rows + 3) // 4 * 4
+
+
 def config_block(cfg, rows_per_rank, args):
+    split = ("proportional slices: 50M / 8 rows per GPU" if cfg.name == "cfg5"
+             and args.scaling == "weak" else
+             f"{args.scaling} scaling: the config's rows split over the GPUs"
+             if args.scaling == "strong" else f"{args.scaling} scaling")
     return {"workload": f"{cfg.name}: {cfg.data}; model: {cfg.model}",
             "rows_per_gpu": rows_per_rank, "features": cfg.features, "trees": cfg.trees,
             "classes": cfg.classes, "output": cfg.output, "parallelism": "row shards",
+            "split": split,
             "l2": "inputs larger than L2 (each step reads every row once)"}
 
 
@@ -316,7 +405,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="cfg2")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
+                    help="default: strong for cfg1-cfg4, proportional slices (weak) for cfg5")
     ap.add_argument("--rows", type=int, default=0, help="override rows per GPU")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--ref-rows", type=int, default=200_000)
@@ -331,6 +421,8 @@ def main():
 
     dist = Dist()
     cfg = synth.CONFIGS[args.config]
+    if args.scaling is None:
+        args.scaling = default_scaling(cfg)
     if args.workload == "contrib":
         run_contrib(args, dist, cfg)
         dist.close()
@@ -355,13 +447,7 @@ def main():
     dev = dist.local_rank
     torch.cuda.set_device(dev)
     affinity = bind_near_gpu(dev) if dist.world > 1 else None
-    if args.rows:
-        rows = args.rows
-    elif args.scaling == "weak":
-        rows = cfg.rows
-    else:
-        rows = cfg.rows // dist.world
-    rows = (rows + 3) // 4 * 4
+    rows = rows_per_rank(cfg, args, dist.world)
     row_start = dist.rank * rows
     kind = OUTPUT_KIND[cfg.output]
     h = _core.load_json(text)
@@ -415,13 +501,23 @@ def main():
     units = rows * cfg.trees * dist.world
     value = units / per_step_s
 
-    # spot-check this rank's device outputs against the oracle on a few rows
-    # is done by the test-suite; here only sanity (finite, in range)
-    out_check = outd[: min(rows, 1000)].cpu().numpy()
-    assert np.isfinite(out_check).all() or cfg.output == "raw"
+    # the step's output, and the raw margins of the same rows (one more
+    # launch, after the timed region), for the parity check of the CPU leg
+    out_gpu = outd.cpu().numpy()
+    raw_gpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        K = cfg.classes
+        rawd = torch.empty((rows, K), dtype=torch.float32, device=f"cuda:{dev}")
+        _core.predict_device(h, dev, xd.data_ptr(), rows, cfg.features, rows, rawd.data_ptr(),
+                             kind=1, stream=stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+        _core.check_device(h, dev)
+        raw_gpu = rawd.cpu().numpy()
+        del rawd
 
     # end to end through the reference-facing C ABI with host buffers
     e2e_s = None
+    ceiling = None
     if args.e2e_steps > 0:
         _core.predict_ex(h, np.asarray(Xh), kind=kind, layout="feature", devices=[dev], out=outh)
         dist.barrier()
@@ -433,6 +529,7 @@ def main():
                              out=outh)
             e2e_times.append(time.perf_counter() - t0)
         e2e_s = dist.max(sum(e2e_times) / len(e2e_times))
+        ceiling = copy_ceiling(dist, dev, stream, rows * S * 4, rows * ocols * 4, e2e_s)
 
     peak, peak_src = measured_peak_hbm()
     alg_bytes = rows * 4 * (S + ocols)
@@ -453,7 +550,10 @@ def main():
                              "the tree walk is bound by shared-memory wavefronts, not HBM"},
         "e2e": None if e2e_s is None else {
             "value": units / e2e_s, "unit": UNIT,
-            "h2d_bytes_per_step": rows * S * 4, "d2h_bytes_per_step": rows * ocols * 4},
+            "h2d_bytes_per_step": rows * S * 4, "d2h_bytes_per_step": rows * ocols * 4,
+            "ms_per_step": e2e_s * 1e3,
+            "frac_of_copy_ceiling": None if ceiling is None else ceiling["copy_ms"] / (e2e_s * 1e3)},
+        "e2e_copy_ceiling": ceiling,
         "gpu_launches": int(launches),
         "clocks": clk,
         "layout": desc,
@@ -461,11 +561,53 @@ def main():
     if affinity:
         line["host_affinity"] = affinity
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, text, cfg.rows)
+        base, raw_o, om = cpu_baseline(cfg, text, np.asarray(Xh))
+        line["cpu_baseline"] = base
+        from oracle import oracle as O
+        line["parity"] = parity_check(O, om, raw_o, raw_gpu, out_gpu, kind)
+        ref = reference_pymodel(cfg, text, np.asarray(Xh))
+        if ref is not None:
+            line["cpu_baseline_reference"] = ref
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     del xd, outd
     dist.close()
+
+
+def copy_ceiling(dist, dev, stream, h2d_bytes, d2h_bytes, e2e_s):
+    """Plain page-locked copies of an e2e step's bytes, every rank at once:
+    H2D of the input and D2H of the output, timed with CUDA events on the
+    bench stream (best of 3 after one warm-up, max over ranks)."""
+    import torch
+    hin = torch.empty(h2d_bytes // 4, dtype=torch.float32, pin_memory=True)
+    din = torch.empty(h2d_bytes // 4, dtype=torch.float32, device=f"cuda:{dev}")
+    hout = torch.empty(max(d2h_bytes // 4, 1), dtype=torch.float32, pin_memory=True)
+    dout = torch.empty(max(d2h_bytes // 4, 1), dtype=torch.float32, device=f"cuda:{dev}")
+
+    def timed(fn):
+        best = None
+        for i in range(4):
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            if i:
+                t = e0.elapsed_time(e1)
+                best = t if best is None else min(best, t)
+        return dist.max(best)
+
+    h2d_ms = timed(lambda: din.copy_(hin, non_blocking=True))
+    d2h_ms = timed(lambda: hout.copy_(dout, non_blocking=True))
+    del hin, din, hout, dout
+    return {"h2d_gbs": h2d_bytes / h2d_ms / 1e6, "d2h_gbs": d2h_bytes / d2h_ms / 1e6,
+            "copy_ms": h2d_ms + d2h_ms, "ranks_copying_at_once": dist.world,
+            "note": "plain cudaMemcpyAsync (torch copy_) of the step's input and output "
+                    "bytes from/to page-locked memory, all ranks at once, max over ranks; "
+                    "e2e.frac_of_copy_ceiling = copy_ms / e2e ms_per_step"}
 
 
 def _time_steps(step, steps, warmup, stream, dist, clocks=None):

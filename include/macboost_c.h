@@ -181,12 +181,13 @@ void macboost_host_free(void *p);
  * The scratch it needs -- a status word and, for row-major input, a
  * feature-major copy of x_dev of at most 16 MiB (4,194,304 values,
  * round_up(rows, 4) * cols) -- is one fixed array inside the library that a
- * GPU keeps from the first use of this call on it until the process exits;
- * larger row-major inputs are rejected with an error (split them, or pass
- * feature-major input, which needs no copy).  Every call shares that array:
- * calls that overlap on the GPU race, so serialise them.  The first call on a
- * device looks up the array's address on that device.  The call waits for its
- * work on `stream` to finish and reports kernel-side errors itself. */
+ * GPU reserves when macboost_prepare sets the model up on it (prepare looks up
+ * the array's address there, which loads the library's module that holds it)
+ * and keeps until the process exits; larger row-major inputs are rejected with
+ * an error (split them, or pass feature-major input, which needs no copy).
+ * Every call shares that array: calls that overlap on the GPU race, so
+ * serialise them.  The call waits for its work on `stream` to finish and
+ * reports kernel-side errors itself. */
 int32_t macboost_predict_device_noalloc(void *handle, int32_t device, const float *x_dev,
                                         int64_t rows, int64_t cols, int64_t ld, int32_t layout,
                                         int32_t kind, void *out_dev, void *stream, char **err);

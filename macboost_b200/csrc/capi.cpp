@@ -130,7 +130,7 @@ int32_t macboost_prepare(void* handle, const int32_t* devices, int32_t ndev, cha
   }
   for (int d : devs) {
     std::string e;
-    if (!mb::engine_prepare(*engine(handle), d, e)) {
+    if (!mb::engine_prepare(*engine(handle), d, e) || mb::noalloc_setup(d, e) != 0) {
       set_error(err, e);
       return -1;
     }

@@ -11,6 +11,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -69,6 +70,29 @@ int ensure(void*& buf, size_t& cap, size_t bytes, std::string& err) {
 // Kernel family: 0 complete, 1 explicit, 2 complete with binned codes.
 int layout_code(const FlatForest& f) { return f.codes ? 2 : int(f.layout); }
 
+// Device-wait settings, read at each launch: MACBOOST_WAIT_LIMIT_US bounds
+// every mbarrier wait of the forest kernels (2 s when unset or invalid), and
+// MACBOOST_TEST_STALL_TILES=1 (a test hook, off by default) makes the row-tile
+// waits run out with no copy in flight, to exercise the abort path.
+void apply_wait_env(KArgs& a) {
+  a.wait_ns = kDefaultWaitNs;
+  if (const char* s = std::getenv("MACBOOST_WAIT_LIMIT_US")) {
+    char* end = nullptr;
+    const long long us = std::strtoll(s, &end, 10);
+    if (end != s && us > 0 && us <= 60000000ll) a.wait_ns = (unsigned long long)us * 1000ull;
+  }
+  const char* st = std::getenv("MACBOOST_TEST_STALL_TILES");
+  a.stall_tiles = (st && st[0] == '1') ? 1 : 0;
+}
+
+// CTAs of one launch over `ntiles` row tiles: one wave of resident CTAs, or
+// fewer under MACBOOST_PLAN "grid".
+int grid_for(const FlatForest& f, const DeviceState& d, int64_t ntiles) {
+  int64_t g = std::min<int64_t>(ntiles, d.grid_ctas);
+  if (f.plan.grid_cap > 0) g = std::min<int64_t>(g, f.plan.grid_cap);
+  return int(std::max<int64_t>(g, 1));
+}
+
 KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   const FlatForest& f = e.flat;
   KArgs a{};
@@ -104,6 +128,7 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.R = f.plan.R;
   a.tile_bufs = f.plan.tile_bufs;
   a.err = d.err;
+  apply_wait_env(a);
   return a;
 }
 
@@ -125,7 +150,7 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
     a.out_leaf = nullptr;
   }
   a.ntiles = (rows + a.R - 1) / a.R;
-  const int grid = int(std::min<int64_t>(a.ntiles, d.grid_ctas));
+  const int grid = grid_for(e.flat, d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
                                  e.flat.plan.smem, grid, s, e.flat.code_bytes, e.top.get());
   if (ce != cudaSuccess) {
@@ -323,6 +348,7 @@ int run_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t c
   const int64_t budget = int64_t(256) << 20;
   int64_t C = std::min(budget / in_row, budget / out_row);
   C = std::max<int64_t>(C / R * R, R);
+  if (f.plan.chunk_rows > 0) C = std::max<int64_t>(f.plan.chunk_rows / 4 * 4, 4);
   if (C > n) C = (n + 3) / 4 * 4;
   const int64_t ldc = (C + 3) / 4 * 4;
   for (int p = 0; p < 2; ++p) {
@@ -535,7 +561,7 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
   a.out_leaf = kind == kKindLeaf ? static_cast<int*>(out) : nullptr;
   a.err = status;
   a.ntiles = (rows + a.R - 1) / a.R;
-  const int grid = int(std::min<int64_t>(a.ntiles, d->grid_ctas));
+  const int grid = grid_for(e.flat, *d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
                                  e.flat.plan.smem, grid, stream, e.flat.code_bytes, e.top.get());
   if (ce != cudaSuccess) {
@@ -665,8 +691,9 @@ int launch_shap_on(Engine& e, DeviceState& d, const float* x, int64_t rows, int6
   a.scratch = d.shap_scratch;
   a.R = d.shap_R;
   a.ntiles = (rows + a.R - 1) / a.R;
-  const int grid = int(std::min<int64_t>(d.shap_grid, a.ntiles));
-  MB_CUDA(launch_shap(a, std::max(s.max_unique, 1), d.shap_in_smem, d.shap_smem, grid, st),
+  int64_t grid = std::min<int64_t>(d.shap_grid, a.ntiles);
+  if (e.flat.plan.grid_cap > 0) grid = std::min<int64_t>(grid, e.flat.plan.grid_cap);
+  MB_CUDA(launch_shap(a, std::max(s.max_unique, 1), d.shap_in_smem, d.shap_smem, int(grid), st),
           "contributions kernel launch");
   g_kernel_launches.fetch_add(1);
   return 0;
@@ -692,6 +719,7 @@ int run_contrib_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, i
   const int64_t budget = int64_t(256) << 20;
   int64_t C = std::min(budget / in_row, budget / out_row);
   C = std::max<int64_t>(C / R * R, R);
+  if (e.flat.plan.chunk_rows > 0) C = std::max<int64_t>(e.flat.plan.chunk_rows / 4 * 4, 4);
   if (C > n) C = (n + 3) / 4 * 4;
   const int64_t ldc = (C + 3) / 4 * 4;
   for (int p = 0; p < 2; ++p) {

@@ -121,6 +121,10 @@ int engine_check_device(Engine& e, int device, std::string& err);
 // `status` word.  Allocates nothing; fails if the model is not resident.
 // `x` is feature-major with stride ld; `use_stage_map`: x holds every model
 // feature (false: only the staged features, in slot order).
+// Resolve the no-alloc entry point's scratch on `device` (noalloc.cu); run
+// by macboost_prepare for each device it prepares.
+int noalloc_setup(int device, std::string& err);
+
 int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, int64_t ld,
                            bool use_stage_map, int kind, void* out, unsigned* status,
                            cudaStream_t stream, std::string& err);

@@ -43,9 +43,11 @@ namespace {
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Optional restriction of the planner's choices from the environment, for
-// tuning: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0" (any subset; 0 = free).
+// tuning and tests: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0,grid=2,chunk=4096"
+// (any subset; 0 = free).
 struct PlanOverride {
-  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1;
+  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0;
+  long chunk = 0;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
     if (!s) return;
@@ -62,6 +64,8 @@ struct PlanOverride {
       else if (key == "planes") planes = int(v);
       else if (key == "codes") codes = int(v);
       else if (key == "top") top = int(v);
+      else if (key == "grid") grid = int(v);
+      else if (key == "chunk") chunk = v;
       p = end;
       while (*p == ',' || *p == ' ') ++p;
     }
@@ -190,6 +194,8 @@ bool make_blocks(int ngroups, int G, size_t max_block,
 
 static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int force_planes);
 
+int plan_grid_cap_from_env() { return std::max(0, PlanOverride().grid); }
+
 bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_planes) {
   const PlanOverride ov;
   FlatForest coded;
@@ -197,14 +203,14 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_p
   const bool codes_ok = ov.codes != 0 && force_planes != 0 && flatten_codes(m, coded, why, ov.G, ov.R);
   if (codes_ok && ov.codes == 1) {
     f = std::move(coded);
-    return true;
-  }
-  if (!flatten_f32(m, f, err, force_planes)) {
+  } else if (!flatten_f32(m, f, err, force_planes)) {
     if (!codes_ok) return false;
     f = std::move(coded);
-    return true;
+  } else if (codes_ok && coded.plan.est_clk_per_row < f.plan.est_clk_per_row) {
+    f = std::move(coded);
   }
-  if (codes_ok && coded.plan.est_clk_per_row < f.plan.est_clk_per_row) f = std::move(coded);
+  f.plan.grid_cap = std::max(0, ov.grid);
+  f.plan.chunk_rows = std::max(0L, ov.chunk);
   return true;
 }
 
@@ -607,6 +613,8 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"full_masks\":" + std::to_string(f.full_masks.size() / 8);
   s += ",\"est_clk_per_row\":" + std::string(est);
   s += ",\"plan\":\"" + f.plan.note + "\"";
+  if (f.plan.grid_cap > 0) s += ",\"grid_cap\":" + std::to_string(f.plan.grid_cap);
+  if (f.plan.chunk_rows > 0) s += ",\"chunk_rows\":" + std::to_string(f.plan.chunk_rows);
   s += "}";
   return s;
 }

@@ -105,6 +105,12 @@ struct LaunchPlan {
   size_t smem = 0;        // dynamic shared memory bytes per CTA
   double est_clk_per_row = 0;  // planner's estimate (SM clocks per row)
   std::string note;
+  // Restrictions from MACBOOST_PLAN (0: none).  grid: at most this many CTAs
+  // per launch, so that every persistent CTA (and warp) loops over several
+  // row tiles even on small inputs; chunk: rows per host chunk of a
+  // host-memory predict (default: 256 MB of staged input or output).
+  int grid_cap = 0;
+  int64_t chunk_rows = 0;
 };
 
 struct FlatForest {
@@ -161,6 +167,10 @@ bool flatten_forest(const Model& m, FlatForest& out, std::string& err, int force
 // the forest does not qualify (too deep, too many distinct thresholds).
 bool flatten_codes(const Model& m, FlatForest& out, std::string& why, int force_G = 0,
                    int force_R = 0);
+
+// The "grid" restriction of MACBOOST_PLAN (0 when unset), for launchers that
+// have no forest plan (the binned-data kernels).
+int plan_grid_cap_from_env();
 
 // Human-readable JSON description of a flattened forest.
 std::string describe_forest(const FlatForest& f);

@@ -59,7 +59,16 @@ struct KArgs {
   int R, tile_bufs;
   long long ntiles;
   unsigned* err;
+  // Bound of every mbarrier wait, in ns of %globaltimer (kDefaultWaitNs
+  // unless MACBOOST_WAIT_LIMIT_US says otherwise).
+  unsigned long long wait_ns;
+  // Test hook (MACBOOST_TEST_STALL_TILES=1, off by default): row-tile
+  // barriers expect their bytes but no copy is issued, so the tile waits run
+  // out with nothing in flight and the abort path is exercised.
+  int stall_tiles;
 };
+
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s
 
 // Complete layout: the records of heap nodes 0, 1 and 2 of every tree, passed
 // by value as a kernel parameter, so the first two levels of the walk read the

@@ -341,7 +341,9 @@ cudaError_t launch_binned(const BinnedArgs& a, cudaStream_t stream) {
     int per_sm = 1;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, R, smem);
     if (e != cudaSuccess) return e;
-    const long long want = (long long)(per_sm < 1 ? 1 : per_sm) * sms;
+    long long want = (long long)(per_sm < 1 ? 1 : per_sm) * sms;
+    const int cap = plan_grid_cap_from_env();  // MACBOOST_PLAN "grid" (tests)
+    if (cap > 0 && want > cap) want = cap;
     const int grid = int(ntiles < want ? ntiles : want);
     k<<<grid, R, smem, stream>>>(b);
     return cudaGetLastError();

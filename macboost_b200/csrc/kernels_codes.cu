@@ -154,23 +154,34 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
     if (a.nblocks > 0) dev::issue_block(a, 0, fbuf, bar_f0, lane);
     if (bulk) dev::issue_tile(a, tile, raw, bar_tile, lane);
   }
+  // Forest blocks consumed (resident forest: 1 once it has landed).  Copies
+  // in flight, for the abort path, follow from the loop state: raw tile copy k
+  // is this CTA's k-th tile (one buffer; tile k + 1 is issued once tile k is
+  // binned), block fseq is in flight until consumed, block fseq + 1 once
+  // prefetched.
   unsigned fseq = 0;
+  const unsigned f_any = a.nblocks > 0 ? 1u : 0u;
   for (int k = 0; tile < a.ntiles; tile += gridDim.x, ++k) {
     const long long next = tile + gridDim.x;
     if (bulk) {
-      const bool ok = dev::mbar_wait(bar_tile, uint32_t(k & 1), a.err);
-      if (__syncthreads_or(!ok)) return;
+      const bool ok = dev::mbar_wait(bar_tile, uint32_t(k & 1), a.err, a.wait_ns);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0)
+          dev::drain_copies(a, bar_f0, fseq, streaming ? fseq + 1 : f_any, bar_tile, 1, k, k + 1);
+        return;
+      }
     } else if (a.S_stage > 0) {
       dev::load_tile_sync(a, tile, raw);
       __syncthreads();
     }
     bin_row<CW>(a, raw_row, code_row);
     __syncthreads();  // the raw tile is consumed: stage the next one during the walk
-    if (bulk && warp == 0 && next < a.ntiles) {
+    if (bulk && next < a.ntiles && warp == 0) {
       if (lane == 0) dev::fence_proxy_async();
       __syncwarp();
       dev::issue_tile(a, next, raw, bar_tile, lane);
     }
+    const int t_issued = k + ((bulk && next < a.ntiles) ? 2 : 1);
     const long long row = tile * a.R + tid;
     dev::Acc<KT> acc;
     acc.init(a.base, a.K);
@@ -178,24 +189,32 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
       uint32_t fb;
       if (streaming) {
         __syncthreads();  // release the buffer of block fseq-1 ...
-        if (warp == 0) {  // ... and prefetch block fseq+1 into it
-          int nb = b + 1;
-          if (nb == a.nblocks) nb = (next < a.ntiles) ? 0 : -1;
-          if (nb >= 0) {
-            if (lane == 0) dev::fence_proxy_async();
-            __syncwarp();
-            dev::issue_block(a, nb, fbuf + ((fseq + 1) & 1) * a.buf_bytes,
-                             bar_f0 + 8u * ((fseq + 1) & 1), lane);
-          }
+        int nb = b + 1;   // ... and prefetch block fseq+1 into it
+        if (nb == a.nblocks) nb = (next < a.ntiles) ? 0 : -1;
+        if (nb >= 0 && warp == 0) {
+          if (lane == 0) dev::fence_proxy_async();
+          __syncwarp();
+          dev::issue_block(a, nb, fbuf + ((fseq + 1) & 1) * a.buf_bytes,
+                           bar_f0 + 8u * ((fseq + 1) & 1), lane);
         }
-        const bool ok = dev::mbar_wait(bar_f0 + 8u * (fseq & 1), (fseq >> 1) & 1, a.err);
-        if (__syncthreads_or(!ok)) return;
+        const bool ok =
+            dev::mbar_wait(bar_f0 + 8u * (fseq & 1), (fseq >> 1) & 1, a.err, a.wait_ns);
+        if (__syncthreads_or(!ok)) {
+          if (tid == 0)
+            dev::drain_copies(a, bar_f0, fseq, fseq + (nb >= 0 ? 2u : 1u), bar_tile, 1, k + 1,
+                              t_issued);
+          return;
+        }
         fb = fbuf + (fseq & 1) * a.buf_bytes;
         ++fseq;
       } else {
         if (k == 0) {
-          const bool ok = dev::mbar_wait(bar_f0, 0, a.err);
-          if (__syncthreads_or(!ok)) return;
+          const bool ok = dev::mbar_wait(bar_f0, 0, a.err, a.wait_ns);
+          if (__syncthreads_or(!ok)) {
+            if (tid == 0) dev::drain_copies(a, bar_f0, 0, 1, bar_tile, 1, k + 1, t_issued);
+            return;
+          }
+          fseq = 1;
         }
         fb = fbuf;
       }

@@ -12,8 +12,6 @@
 namespace mb {
 namespace dev {
 
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
-
 // Threads per CTA the kernels are compiled for (mb::max_threads_for_group):
 // groups of 10 or more trees, and more than two classes' accumulators, need
 // the larger per-thread register budget of fewer threads.
@@ -100,13 +98,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for phase `parity`; false (and *err |= timeout) after 2 s.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* err) {
+// Bounded wait for phase `parity`; false (and *err |= timeout) after
+// `limit_ns` of %globaltimer.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned* err,
+                                          unsigned long long limit_ns = kDefaultWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       atomicOr(err, kErrWaitTimeout);
       return false;
     }
@@ -115,6 +115,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
 
 // Warp 0: stage the staged slots of row tile `tile` with bulk copies, one per
 // slot: R consecutive values of one feature (16-byte aligned, multiple of 16).
+// With the stall hook the barrier expects the bytes but no copy is issued.
 __device__ __forceinline__ void issue_tile(const KArgs& a, long long tile, uint32_t dst,
                                            uint32_t bar, int lane) {
   const long long r0 = tile * a.R;
@@ -123,6 +124,7 @@ __device__ __forceinline__ void issue_tile(const KArgs& a, long long tile, uint3
   const uint32_t nbytes = uint32_t(((nv + 3) & ~3ll) * 4);
   if (lane == 0) mbar_arrive_expect_tx(bar, nbytes * uint32_t(a.S_stage));
   __syncwarp();
+  if (a.stall_tiles) return;
   for (int s = lane; s < a.S_stage; s += 32) {
     const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
     bulk_g2s(dst + uint32_t(s) * uint32_t(a.R) * 4u, a.x + f * a.ld + r0, nbytes, bar);
@@ -304,6 +306,30 @@ __device__ __forceinline__ void epilogue(const KArgs& a, const Acc<KT>& acc, lon
   for (int c = 0; c < K; ++c) o[row * K + c] = acc.get(c);
 }
 
+// Barrier and phase of the j-th row-tile copy a CTA (or warp) issues: copies
+// alternate between two buffers, each with its own barrier, or reuse one.
+__device__ __forceinline__ uint32_t copy_bar(uint32_t bar0, int bufs, int j) {
+  return bufs == 2 ? bar0 + 8u * uint32_t(j & 1) : bar0;
+}
+__device__ __forceinline__ uint32_t copy_parity(int bufs, int j) {
+  return bufs == 2 ? uint32_t((j >> 1) & 1) : uint32_t(j & 1);
+}
+
+// The abort path's last step: before a CTA (or warp) that gave up returns,
+// one thread waits, bounded, for every bulk copy it issued and did not
+// consume -- the one that timed out included -- so that no copy can still be
+// writing this CTA's shared memory once it has exited.  Forest block copy i
+// completes phase (i >> 1) & 1 of barrier bar_f0 + 8 (i & 1); row-tile copies
+// as copy_bar / copy_parity.  The status word already holds the timeout.
+static __device__ __noinline__ void drain_copies(const KArgs& a, uint32_t bar_f0, unsigned f_cons,
+                                             unsigned f_issued, uint32_t bar_t0, int bufs,
+                                             int t_cons, int t_issued) {
+  for (unsigned i = f_cons; i < f_issued; ++i)
+    mbar_wait(bar_f0 + 8u * (i & 1u), (i >> 1) & 1u, a.err, a.wait_ns);
+  for (int j = t_cons; j < t_issued; ++j)
+    mbar_wait(copy_bar(bar_t0, bufs, j), copy_parity(bufs, j), a.err, a.wait_ns);
+}
+
 // The per-CTA pipeline shared by both layouts: a persistent loop over row
 // tiles (double- or single-buffered bulk staging), forest blocks (resident,
 // or streamed through two buffers), the -Inf plane fill, and the bounded-wait
@@ -340,23 +366,36 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
     if (a.nblocks > 0) issue_block(a, 0, fbuf, bar_f0, lane);
     if (bulk) issue_tile(a, tile, tiles, bar_tile0, lane);
   }
-  unsigned fseq = 0;  // forest blocks consumed by this CTA
+  // Forest blocks consumed by this CTA (resident forest: 1 once it has
+  // landed).  Copies in flight, for the abort path, follow from the loop
+  // state: tile copy k is this CTA's k-th tile; tile k + 1 is in flight during
+  // iteration k when it is double-buffered; block fseq of the forest is in
+  // flight until consumed, and block fseq + 1 once prefetched.
+  unsigned fseq = 0;
+  const unsigned f_any = a.nblocks > 0 ? 1u : 0u;
 
   for (int k = 0; tile < a.ntiles; tile += gridDim.x, ++k) {
     const int tb = (a.tile_bufs == 2) ? (k & 1) : 0;
     const uint32_t tl = tiles + uint32_t(tb) * a.tile_bytes;
     const long long next = tile + gridDim.x;
-    if (bulk && a.tile_bufs == 2 && warp == 0 && next < a.ntiles) {
+    const bool ahead = bulk && a.tile_bufs == 2 && next < a.ntiles;
+    if (ahead && warp == 0) {
       // buffer tb^1 held tile k-1, released by the barrier ending that iteration
       if (lane == 0) fence_proxy_async();
       __syncwarp();
       issue_tile(a, next, tiles + uint32_t(tb ^ 1) * a.tile_bytes, bar_tile0 + 8u * (tb ^ 1),
                  lane);
     }
+    const int t_issued = k + (ahead ? 2 : 1);
     if (bulk) {
-      const uint32_t parity = (a.tile_bufs == 2) ? uint32_t((k >> 1) & 1) : uint32_t(k & 1);
-      const bool ok = mbar_wait(bar_tile0 + 8u * tb, parity, a.err);
-      if (__syncthreads_or(!ok)) return;
+      const bool ok = mbar_wait(copy_bar(bar_tile0, a.tile_bufs, k),
+                                copy_parity(a.tile_bufs, k), a.err, a.wait_ns);
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0)
+          drain_copies(a, bar_f0, fseq, streaming ? fseq + 1 : f_any, bar_tile0, a.tile_bufs, k,
+                       t_issued);
+        return;
+      }
     } else if (a.S_stage > 0) {
       load_tile_sync(a, tile, tl);
       __syncthreads();
@@ -385,24 +424,31 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
       if (streaming) {
         // release the buffer of block fseq-1, then prefetch block fseq+1 into it
         __syncthreads();
-        if (warp == 0) {
-          int nb = b + 1;
-          if (nb == a.nblocks) nb = (next < a.ntiles) ? 0 : -1;
-          if (nb >= 0) {
-            if (lane == 0) fence_proxy_async();
-            __syncwarp();
-            issue_block(a, nb, fbuf + ((fseq + 1) & 1) * a.buf_bytes,
-                        bar_f0 + 8u * ((fseq + 1) & 1), lane);
-          }
+        int nb = b + 1;
+        if (nb == a.nblocks) nb = (next < a.ntiles) ? 0 : -1;
+        if (nb >= 0 && warp == 0) {
+          if (lane == 0) fence_proxy_async();
+          __syncwarp();
+          issue_block(a, nb, fbuf + ((fseq + 1) & 1) * a.buf_bytes,
+                      bar_f0 + 8u * ((fseq + 1) & 1), lane);
         }
-        const bool ok = mbar_wait(bar_f0 + 8u * (fseq & 1), (fseq >> 1) & 1, a.err);
-        if (__syncthreads_or(!ok)) return;
+        const bool ok = mbar_wait(bar_f0 + 8u * (fseq & 1), (fseq >> 1) & 1, a.err, a.wait_ns);
+        if (__syncthreads_or(!ok)) {
+          if (tid == 0)
+            drain_copies(a, bar_f0, fseq, fseq + (nb >= 0 ? 2u : 1u), bar_tile0, a.tile_bufs,
+                         k + 1, t_issued);
+          return;
+        }
         fb = fbuf + (fseq & 1) * a.buf_bytes;
         ++fseq;
       } else {
         if (k == 0) {
-          const bool ok = mbar_wait(bar_f0, 0, a.err);
-          if (__syncthreads_or(!ok)) return;
+          const bool ok = mbar_wait(bar_f0, 0, a.err, a.wait_ns);
+          if (__syncthreads_or(!ok)) {
+            if (tid == 0) drain_copies(a, bar_f0, 0, 1, bar_tile0, a.tile_bufs, k + 1, t_issued);
+            return;
+          }
+          fseq = 1;
         }
         fb = fbuf;
       }
@@ -410,7 +456,7 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
     }
     if (row < a.rows) epilogue<KT>(a, acc, row);
     __syncthreads();  // every thread is done with tile buffer tb
-    if (bulk && a.tile_bufs == 1 && warp == 0 && next < a.ntiles) {
+    if (bulk && a.tile_bufs == 1 && next < a.ntiles && warp == 0) {
       if (lane == 0) fence_proxy_async();
       __syncwarp();
       issue_tile(a, next, tiles, bar_tile0, lane);
@@ -421,14 +467,20 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
 // The per-warp pipeline, for a forest resident in shared memory (one block):
 // each warp stages and scores its own chunks of 32 rows, independently of the
 // other warps of the CTA.  Chunk c covers rows [32c, 32c + 32); warp w of CTA
-// b takes chunks (b * W + w) + k * gridDim.x * W, so the chunks in flight at
-// any time form one contiguous run of rows.  A chunk lands, one bulk copy of
-// 128 bytes per staged slot, in the warp's 32 columns of the row-tile layout
-// (slot s, row j of the warp at tile + 4 * (s * R + 32 w + j)), on the warp's
-// own mbarrier.  With two tile buffers the next chunk is in flight while the
-// current one is scored; with one, the next copy is issued when the warp is
-// done, and the other warps keep the SM busy meanwhile.  No CTA-wide barrier
-// follows the forest wait, and a chunk's NaN test is a warp vote.
+// b takes chunks (w * gridDim.x + b) + k * gridDim.x * W, so the chunks in
+// flight at any time form one contiguous run of rows, and the chunks left
+// over after the last full pass over all warps fall to warps of every CTA
+// alike (each CTA's count differs from another's by at most one), not to the
+// first CTAs only: with few chunks per warp (a row slice of one GPU of
+// several) that keeps every SM's share within one chunk of the others.  A
+// chunk lands, one bulk copy of 128 bytes per staged slot, in the warp's 32
+// columns of the row-tile layout (slot s, row j of the warp at
+// tile + 4 * (s * R + 32 w + j)), on the warp's own mbarrier.  With two tile
+// buffers the next chunk is in flight while the current one is scored; with
+// one, the next copy is issued when the warp is done, and the other warps keep
+// the SM busy meanwhile.  No CTA-wide barrier follows the forest wait, and a
+// chunk's NaN test is a warp vote.  A warp that gives up waiting drains its own
+// copies (drain_copies) and returns; the other warps go on with theirs.
 template <int KT, bool CHECK_NAN = false, class ScoreBlock>
 __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, ScoreBlock score) {
   const int tid = threadIdx.x;
@@ -443,7 +495,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
   const bool bulk = a.bulk && a.S_stage > 0;
   const long long nchunks = (a.rows + 31) / 32;
   const long long stride = (long long)gridDim.x * W;
-  long long c = (long long)blockIdx.x * W + warp;
+  long long c = (long long)warp * gridDim.x + blockIdx.x;
 
   if (tid == 0) {
     mbar_init(bar_f0, 1);
@@ -460,7 +512,10 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
               -__int_as_float(0x7f800000));
   }
   __syncthreads();
-  if (c >= nchunks) return;  // warp 0 has the CTA's first chunk: nothing was issued
+  // Warp 0 holds the CTA's lowest chunk (b): when it has none, no warp of the
+  // CTA has one and nothing was issued; when it has one, it stages the forest,
+  // which every warp that gets past here can then wait for.
+  if (c >= nchunks) return;
   if (warp == 0) issue_block(a, 0, fbuf, bar_f0, lane);
 
   auto issue = [&](long long cc, int buf) {
@@ -471,6 +526,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
     const uint32_t bar = bar_w + 8u * uint32_t(buf);
     if (lane == 0) mbar_arrive_expect_tx(bar, nbytes * uint32_t(a.S_stage));
     __syncwarp();
+    if (a.stall_tiles) return;  // test hook: the bytes never come
     const uint32_t dst = tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u;
     for (int s = lane; s < a.S_stage; s += 32) {
       const long long f = a.stage_feature ? __ldg(a.stage_feature + s) : s;
@@ -484,6 +540,8 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
     __syncwarp();
   };
 
+  // Chunk copy k is this warp's k-th chunk; during iteration k, copy k + 1 is
+  // in flight when it was issued ahead (two buffers).
   if (bulk) issue(c, 0);
   bool forest_ready = false;
   for (int k = 0; c < nchunks; c += stride, ++k) {
@@ -494,14 +552,15 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       release();  // buffer buf^1 held chunk k-1
       issue(cn, buf ^ 1);
     }
+    const int k_issued = k + (ahead ? 2 : 1);
     const uint32_t rowbase = tiles + uint32_t(buf) * a.tile_bytes + uint32_t(tid) * 4u;
     const long long row = c * 32 + lane;
     if (bulk) {
-      const uint32_t parity = (a.tile_bufs == 2) ? uint32_t((k >> 1) & 1) : uint32_t(k & 1);
-      const bool ok = mbar_wait(bar_w + 8u * uint32_t(buf), parity, a.err);
+      const bool ok = mbar_wait(copy_bar(bar_w, a.tile_bufs, k), copy_parity(a.tile_bufs, k),
+                                a.err, a.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
-        // the copy of chunk k+1 may still be in flight: let it land (bounded)
-        if (ahead) mbar_wait(bar_w + 8u * uint32_t(buf ^ 1), uint32_t(((k + 1) >> 1) & 1), a.err);
+        if (lane == 0) drain_copies(a, bar_f0, forest_ready ? 1u : 0u, 1u, bar_w, a.tile_bufs, k, k_issued);
+        __syncwarp();
         return;
       }
     } else {
@@ -513,9 +572,10 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       __syncwarp();
     }
     if (!forest_ready) {
-      const bool ok = mbar_wait(bar_f0, 0, a.err);
+      const bool ok = mbar_wait(bar_f0, 0, a.err, a.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
-        if (ahead) mbar_wait(bar_w + 8u * uint32_t(buf ^ 1), uint32_t(((k + 1) >> 1) & 1), a.err);
+        if (lane == 0) drain_copies(a, bar_f0, 0u, 1u, bar_w, a.tile_bufs, k + 1, k_issued);
+        __syncwarp();
         return;
       }
       forest_ready = true;

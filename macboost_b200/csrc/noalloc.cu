@@ -61,6 +61,32 @@ void set_error(char** err, const std::string& msg) {
 
 }  // namespace
 
+namespace mb {
+
+// Set-up for this entry point on `device`, run by macboost_prepare: looking up
+// the scratch's address loads this file's module on that device, which is
+// when the GPU reserves the array, so no no-alloc call is the one that
+// reserves it.
+int noalloc_setup(int device, std::string& err) {
+  if (device < 0 || device >= kMaxDevices) {
+    err = "device " + std::to_string(device) + " is out of range for the no-alloc scratch";
+    return -1;
+  }
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    err = "cannot make device " + std::to_string(device) + " current";
+    return -1;
+  }
+  void* p = nullptr;
+  const int rc = scratch_address(device, &p, err);
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  return rc;
+}
+
+}  // namespace mb
+
 // (the .cu files are compiled with hidden visibility; this one is exported)
 extern "C" __attribute__((visibility("default"))) int32_t macboost_predict_device_noalloc(void* handle, int32_t device,
                                                    const float* x_dev, int64_t rows,

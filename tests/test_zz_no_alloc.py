@@ -38,7 +38,14 @@ class _DeviceMemory:
         self.lib.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
                                         ctypes.c_int]
         self.lib.cudaFree.argtypes = [ctypes.c_void_p]
+        self.lib.cudaMemGetInfo.argtypes = [ctypes.POINTER(ctypes.c_size_t),
+                                            ctypes.POINTER(ctypes.c_size_t)]
         self.ptrs = []
+
+    def free_bytes(self):
+        free, total = ctypes.c_size_t(), ctypes.c_size_t()
+        assert self.lib.cudaMemGetInfo(ctypes.byref(free), ctypes.byref(total)) == 0
+        return free.value
 
     def upload(self, a):
         p = ctypes.c_void_p()
@@ -97,6 +104,12 @@ def test_noalloc_matches_allocating_entry_point(gpu, kind):
         core.predict_device(h, 0, dx, rows, F, ld, dref, kind=kind)
         core.check_device(h, 0)
         ref = mem.download(dref, (rows, ncol), np.float32)
+        # one call per layout first: the kernels' modules load (and the driver
+        # reserves their memory) on first use; after that the free device
+        # memory must not move while the entry point runs
+        _call(core, h, dx, rows, F, ld, 0, kind, dout)
+        _call(core, h, dxr, rows, F, 0, 1, kind, dout)
+        free0 = mem.free_bytes()
         for layout, x, stride in [(0, dx, ld), (0, dx, ld), (1, dxr, 0), (1, dxr, 0)]:
             _call(core, h, x, rows, F, stride, layout, kind, dout)
             got = mem.download(dout, (rows, ncol), np.float32)
@@ -104,6 +117,7 @@ def test_noalloc_matches_allocating_entry_point(gpu, kind):
                 assert_bitwise(got, ref, f"no-alloc layout={layout}")
             else:
                 assert_ulp(got, ref, 2, f"no-alloc layout={layout}")
+        assert mem.free_bytes() == free0, "the no-alloc entry point changed free device memory"
     finally:
         mem.free()
 
