@@ -85,6 +85,21 @@ void apply_wait_env(KArgs& a) {
   a.stall_tiles = (st && st[0] == '1') ? 1 : 0;
 }
 
+// The per-warp pipeline's chunk counters for launches on `s`: a pair of its
+// own per stream, since launches on one stream never overlap and each leaves
+// its pair at zero.  The per-thread default stream names a different stream
+// on every host thread, so it (and a stream beyond the pool) gets none: the
+// kernel then takes chunks in a fixed order.
+unsigned long long* sched_for(DeviceState& d, cudaStream_t s) {
+  if (d.sched == nullptr || s == cudaStreamPerThread) return nullptr;
+  std::lock_guard<std::mutex> lk(d.sched_mu);
+  for (size_t i = 0; i < d.sched_streams.size(); ++i)
+    if (d.sched_streams[i] == s) return d.sched + 2 * i;
+  if (d.sched_streams.size() >= size_t(kSchedSlots)) return nullptr;
+  d.sched_streams.push_back(s);
+  return d.sched + 2 * (d.sched_streams.size() - 1);
+}
+
 // CTAs of one launch over `ntiles` row tiles: one wave of resident CTAs, or
 // fewer under MACBOOST_PLAN "grid".
 int grid_for(const FlatForest& f, const DeviceState& d, int64_t ntiles) {
@@ -150,6 +165,7 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
     a.out_leaf = nullptr;
   }
   a.ntiles = (rows + a.R - 1) / a.R;
+  a.sched = sched_for(d, s);
   const int grid = grid_for(e.flat, d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
                                  e.flat.plan.smem, grid, s, e.flat.code_bytes, e.top.get());
@@ -173,7 +189,8 @@ DeviceState::~DeviceState() {
                   static_cast<void*>(conv_src), static_cast<void*>(conv_dst),
                   static_cast<void*>(search), static_cast<void*>(bin_plan),
                   static_cast<void*>(masks), static_cast<void*>(leaf_heap),
-                  static_cast<void*>(base), static_cast<void*>(err), shap_paths, shap_uniq,
+                  static_cast<void*>(base), static_cast<void*>(err), static_cast<void*>(sched),
+                  shap_paths, shap_uniq,
                   static_cast<void*>(shap_masks), static_cast<void*>(shap_block_path),
                   static_cast<void*>(shap_block_uniq), static_cast<void*>(shap_class_block),
                   static_cast<void*>(shap_coef), static_cast<void*>(shap_feature_slot),
@@ -288,6 +305,12 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   if ((ce = cudaMalloc(reinterpret_cast<void**>(&d->err), sizeof(unsigned))) != cudaSuccess ||
       (ce = cudaMemset(d->err, 0, sizeof(unsigned))) != cudaSuccess) {
     err = cuda_msg("cudaMalloc (error word)", ce);
+    return nullptr;
+  }
+  const size_t sched_bytes = size_t(kSchedSlots) * 2 * sizeof(unsigned long long);
+  if ((ce = cudaMalloc(reinterpret_cast<void**>(&d->sched), sched_bytes)) != cudaSuccess ||
+      (ce = cudaMemset(d->sched, 0, sched_bytes)) != cudaSuccess) {
+    err = cuda_msg("cudaMalloc (chunk counters)", ce);
     return nullptr;
   }
   for (int i = 0; i < 2; ++i)
@@ -537,7 +560,7 @@ int engine_check_device(Engine& e, int device, std::string& err) {
 
 int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, int64_t ld,
                            bool use_stage_map, int kind, void* out, unsigned* status,
-                           cudaStream_t stream, std::string& err) {
+                           unsigned long long* sched, cudaStream_t stream, std::string& err) {
   DeviceState* d = nullptr;
   {
     std::lock_guard<std::mutex> lk(e.mu);
@@ -560,6 +583,7 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
   a.out = kind == kKindLeaf ? nullptr : static_cast<float*>(out);
   a.out_leaf = kind == kKindLeaf ? static_cast<int*>(out) : nullptr;
   a.err = status;
+  a.sched = sched;
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = grid_for(e.flat, *d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,

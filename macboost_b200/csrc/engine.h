@@ -37,6 +37,12 @@ struct DeviceState {
   int* leaf_heap = nullptr;
   float* base = nullptr;
   unsigned* err = nullptr;              // kernel error word
+  // Row-chunk counters of the per-warp pipeline, one pair per stream that
+  // launches on this replica (launches on one stream run one after another;
+  // each launch leaves its pair at zero): kSchedSlots x {next, done}.
+  unsigned long long* sched = nullptr;
+  std::vector<cudaStream_t> sched_streams;
+  std::mutex sched_mu;
   // staging for host-memory inputs (double-buffered chunks)
   float* xbuf[2] = {nullptr, nullptr};  // feature-major chunk
   size_t xcap[2] = {0, 0};
@@ -116,17 +122,19 @@ int engine_contrib_device(Engine& e, int device, const float* x, int64_t rows, i
 // Synchronise `device` and report any kernel-side error since the last check.
 int engine_check_device(Engine& e, int device, std::string& err);
 
-// Enqueue the forest kernel on a device where the model is already resident
-// (engine_prepare ran before), reporting kernel-side errors into the caller's
-// `status` word.  Allocates nothing; fails if the model is not resident.
-// `x` is feature-major with stride ld; `use_stage_map`: x holds every model
-// feature (false: only the staged features, in slot order).
 // Resolve the no-alloc entry point's scratch on `device` (noalloc.cu); run
 // by macboost_prepare for each device it prepares.
 int noalloc_setup(int device, std::string& err);
 
+// Enqueue the forest kernel on a device where the model is already resident
+// (engine_prepare ran before), reporting kernel-side errors into the caller's
+// `status` word and taking row chunks from the caller's `sched` counters (two
+// zeroed 64-bit words that only launches serialised with this one use; null:
+// a fixed chunk order).  Allocates nothing; fails if the model is not
+// resident.  `x` is feature-major with stride ld; `use_stage_map`: x holds
+// every model feature (false: only the staged features, in slot order).
 int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, int64_t ld,
                            bool use_stage_map, int kind, void* out, unsigned* status,
-                           cudaStream_t stream, std::string& err);
+                           unsigned long long* sched, cudaStream_t stream, std::string& err);
 
 }  // namespace mb

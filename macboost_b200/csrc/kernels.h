@@ -66,7 +66,13 @@ struct KArgs {
   // barriers expect their bytes but no copy is issued, so the tile waits run
   // out with nothing in flight and the abort path is exercised.
   int stall_tiles;
+  // Per-warp pipeline: {next, done} counters from which warps claim row
+  // chunks after their first (zero at launch, zero again when the last warp
+  // leaves), or null for the fixed order c + k * gridDim.x * warps.
+  unsigned long long* sched;
 };
+
+constexpr int kSchedSlots = 256;  // counter pairs per device replica (streams)
 
 constexpr unsigned long long kDefaultWaitNs = 2000000000ull;  // 2 s
 

@@ -467,12 +467,10 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
 // The per-warp pipeline, for a forest resident in shared memory (one block):
 // each warp stages and scores its own chunks of 32 rows, independently of the
 // other warps of the CTA.  Chunk c covers rows [32c, 32c + 32); warp w of CTA
-// b takes chunks (w * gridDim.x + b) + k * gridDim.x * W, so the chunks in
-// flight at any time form one contiguous run of rows, and the chunks left
-// over after the last full pass over all warps fall to warps of every CTA
-// alike (each CTA's count differs from another's by at most one), not to the
-// first CTAs only: with few chunks per warp (a row slice of one GPU of
-// several) that keeps every SM's share within one chunk of the others.  A
+// b starts with chunk w * gridDim.x + b and claims its next chunks from the
+// launch's counters in row order (claim below), so the chunks in flight at
+// any time form one contiguous run of rows and the work evens out across SMs
+// and warps however fast each runs.  A
 // chunk lands, one bulk copy of 128 bytes per staged slot, in the warp's 32
 // columns of the row-tile layout (slot s, row j of the warp at
 // tile + 4 * (s * R + 32 w + j)), on the warp's own mbarrier.  With two tile
@@ -512,10 +510,37 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
               -__int_as_float(0x7f800000));
   }
   __syncthreads();
+  // Chunks after a warp's first: claimed from the launch's counter pair when
+  // there is one (warps that finish early take more chunks, so every SM and
+  // every warp ends within about one chunk of the others, whatever the SMs'
+  // speeds), else the fixed order c + k * stride.  Claims return stride +
+  // next++; a warp stops at its first claim past the last chunk.  Every warp
+  // counts itself out in `done` as it leaves (the claims it made come first,
+  // __threadfence), and the last one out of the grid sets both counters back
+  // to zero for the next launch on its stream.
+  auto claim = [&](long long cur) -> long long {
+    if (a.sched == nullptr) return cur + stride;
+    unsigned long long v = 0;
+    if (lane == 0) v = atomicAdd(a.sched, 1ull);
+    return stride + (long long)__shfl_sync(0xffffffffu, v, 0);
+  };
+  auto leave = [&]() {
+    if (a.sched != nullptr && lane == 0) {
+      __threadfence();
+      const unsigned long long n = atomicAdd(a.sched + 1, 1ull);
+      if (n + 1 == (unsigned long long)gridDim.x * (unsigned long long)W) {
+        atomicExch(a.sched, 0ull);
+        atomicExch(a.sched + 1, 0ull);
+      }
+    }
+  };
   // Warp 0 holds the CTA's lowest chunk (b): when it has none, no warp of the
   // CTA has one and nothing was issued; when it has one, it stages the forest,
   // which every warp that gets past here can then wait for.
-  if (c >= nchunks) return;
+  if (c >= nchunks) {
+    leave();
+    return;
+  }
   if (warp == 0) issue_block(a, 0, fbuf, bar_f0, lane);
 
   auto issue = [&](long long cc, int buf) {
@@ -544,9 +569,10 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
   // in flight when it was issued ahead (two buffers).
   if (bulk) issue(c, 0);
   bool forest_ready = false;
-  for (int k = 0; c < nchunks; c += stride, ++k) {
+  long long cn = 0;
+  for (int k = 0; c < nchunks; c = cn, ++k) {
     const int buf = (a.tile_bufs == 2) ? (k & 1) : 0;
-    const long long cn = c + stride;
+    cn = claim(c);  // its latency overlaps this chunk's walk
     const bool ahead = bulk && a.tile_bufs == 2 && cn < nchunks;
     if (ahead) {
       release();  // buffer buf^1 held chunk k-1
@@ -561,6 +587,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) drain_copies(a, bar_f0, forest_ready ? 1u : 0u, 1u, bar_w, a.tile_bufs, k, k_issued);
         __syncwarp();
+        leave();
         return;
       }
     } else {
@@ -576,6 +603,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) drain_copies(a, bar_f0, 0u, 1u, bar_w, a.tile_bufs, k + 1, k_issued);
         __syncwarp();
+        leave();
         return;
       }
       forest_ready = true;
@@ -604,6 +632,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       issue(cn, 0);
     }
   }
+  leave();
 }
 
 // The pipeline for the forest block layout: per-warp chunks when the forest

@@ -10,7 +10,8 @@
 // point, which allocates nothing.
 //
 // The scratch it needs lives in one file-scope __device__ array below: a
-// status word the kernel reports waiting failures into, and room for the
+// status word the kernel reports waiting failures into, the kernel's two
+// row-chunk counters (which every launch leaves at zero), and room for the
 // feature-major copy of row-major input (at most kRowMajorBytes).  Every GPU
 // that loads this module keeps the array until the process exits.  All calls
 // share it and it keeps the previous call's contents, so each call clears the
@@ -151,6 +152,9 @@ extern "C" __attribute__((visibility("default"))) int32_t macboost_predict_devic
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* status = static_cast<unsigned*>(base);
+  // the kernel's chunk counters: zero in a fresh module, left at zero by
+  // every launch that used them
+  auto* sched = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(base) + 16);
   auto* xt = reinterpret_cast<float*>(static_cast<unsigned char*>(base) + kStatusBytes);
   cudaError_t ce = cudaMemsetAsync(status, 0, sizeof(unsigned), s);  // left over from the last call
   int rc = 0;
@@ -163,12 +167,12 @@ extern "C" __attribute__((visibility("default"))) int32_t macboost_predict_devic
       msg = std::string("transpose launch: ") + cudaGetErrorString(ce);
       rc = -1;
     } else {
-      rc = mb::engine_launch_resident(e, device, xt, rows, ldt, true, kind, out_dev, status, s,
-                                      msg);
+      rc = mb::engine_launch_resident(e, device, xt, rows, ldt, true, kind, out_dev, status,
+                                      sched, s, msg);
     }
   } else {
-    rc = mb::engine_launch_resident(e, device, x_dev, rows, ld, true, kind, out_dev, status, s,
-                                    msg);
+    rc = mb::engine_launch_resident(e, device, x_dev, rows, ld, true, kind, out_dev, status,
+                                    sched, s, msg);
   }
   if (rc == 0) {
     unsigned word = 0;
