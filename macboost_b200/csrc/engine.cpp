@@ -90,8 +90,8 @@ void apply_wait_env(KArgs& a) {
 // its pair at zero.  The per-thread default stream names a different stream
 // on every host thread, so it (and a stream beyond the pool) gets none: the
 // kernel then takes chunks in a fixed order.
-unsigned long long* sched_for(DeviceState& d, cudaStream_t s) {
-  if (d.sched == nullptr || s == cudaStreamPerThread) return nullptr;
+unsigned long long* sched_for(const Engine& e, DeviceState& d, cudaStream_t s) {
+  if (d.sched == nullptr || s == cudaStreamPerThread || !e.flat.plan.claim) return nullptr;
   std::lock_guard<std::mutex> lk(d.sched_mu);
   for (size_t i = 0; i < d.sched_streams.size(); ++i)
     if (d.sched_streams[i] == s) return d.sched + 2 * i;
@@ -165,7 +165,7 @@ int launch(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
     a.out_leaf = nullptr;
   }
   a.ntiles = (rows + a.R - 1) / a.R;
-  a.sched = sched_for(d, s);
+  a.sched = sched_for(e, d, s);
   const int grid = grid_for(e.flat, d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,
                                  e.flat.plan.smem, grid, s, e.flat.code_bytes, e.top.get());
@@ -583,7 +583,7 @@ int engine_launch_resident(Engine& e, int device, const float* x, int64_t rows, 
   a.out = kind == kKindLeaf ? nullptr : static_cast<float*>(out);
   a.out_leaf = kind == kKindLeaf ? static_cast<int*>(out) : nullptr;
   a.err = status;
-  a.sched = sched;
+  a.sched = e.flat.plan.claim ? sched : nullptr;
   a.ntiles = (rows + a.R - 1) / a.R;
   const int grid = grid_for(e.flat, *d, a.ntiles);
   cudaError_t ce = launch_forest(layout_code(e.flat), e.flat.plan.planes, e.model.any_cat, a,

@@ -43,10 +43,10 @@ namespace {
 inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Optional restriction of the planner's choices from the environment, for
-// tuning and tests: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0,grid=2,chunk=4096"
+// tuning and tests: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0,grid=2,chunk=4096,claim=0"
 // (any subset; 0 = free).
 struct PlanOverride {
-  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0;
+  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0, claim = -1;
   long chunk = 0;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
@@ -65,6 +65,7 @@ struct PlanOverride {
       else if (key == "codes") codes = int(v);
       else if (key == "top") top = int(v);
       else if (key == "grid") grid = int(v);
+      else if (key == "claim") claim = int(v);
       else if (key == "chunk") chunk = v;
       p = end;
       while (*p == ',' || *p == ' ') ++p;
@@ -211,6 +212,7 @@ bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_p
   }
   f.plan.grid_cap = std::max(0, ov.grid);
   f.plan.chunk_rows = std::max(0L, ov.chunk);
+  f.plan.claim = ov.claim != 0;
   return true;
 }
 
@@ -615,6 +617,7 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"plan\":\"" + f.plan.note + "\"";
   if (f.plan.grid_cap > 0) s += ",\"grid_cap\":" + std::to_string(f.plan.grid_cap);
   if (f.plan.chunk_rows > 0) s += ",\"chunk_rows\":" + std::to_string(f.plan.chunk_rows);
+  if (!f.plan.claim) s += ",\"claim\":false";
   s += "}";
   return s;
 }

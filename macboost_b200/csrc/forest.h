@@ -111,6 +111,9 @@ struct LaunchPlan {
   // host-memory predict (default: 256 MB of staged input or output).
   int grid_cap = 0;
   int64_t chunk_rows = 0;
+  // Row chunks (tiles) after each warp's (CTA's) first are claimed from
+  // per-stream counters; "claim=0" fixes the order instead.
+  bool claim = true;
 };
 
 struct FlatForest {

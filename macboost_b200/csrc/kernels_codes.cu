@@ -148,8 +148,13 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
     dev::fence_mbar_init();
   }
   __syncthreads();
+  const dev::TileOrder order{a, base + 64u};
   long long tile = blockIdx.x;
-  if (tile >= a.ntiles) return;  // uniform over the CTA
+  if (tile >= a.ntiles) {  // uniform over the CTA
+    order.leave();
+    return;
+  }
+  long long next = tile + gridDim.x;
   if (warp == 0) {
     if (a.nblocks > 0) dev::issue_block(a, 0, fbuf, bar_f0, lane);
     if (bulk) dev::issue_tile(a, tile, raw, bar_tile, lane);
@@ -161,13 +166,14 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
   // prefetched.
   unsigned fseq = 0;
   const unsigned f_any = a.nblocks > 0 ? 1u : 0u;
-  for (int k = 0; tile < a.ntiles; tile += gridDim.x, ++k) {
-    const long long next = tile + gridDim.x;
+  for (int k = 0; tile < a.ntiles; ++k) {
+    order.claim_ahead(k);  // read after the barrier that follows the binning
     if (bulk) {
       const bool ok = dev::mbar_wait(bar_tile, uint32_t(k & 1), a.err, a.wait_ns);
       if (__syncthreads_or(!ok)) {
         if (tid == 0)
           dev::drain_copies(a, bar_f0, fseq, streaming ? fseq + 1 : f_any, bar_tile, 1, k, k + 1);
+        order.leave();
         return;
       }
     } else if (a.S_stage > 0) {
@@ -203,6 +209,7 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
           if (tid == 0)
             dev::drain_copies(a, bar_f0, fseq, fseq + (nb >= 0 ? 2u : 1u), bar_tile, 1, k + 1,
                               t_issued);
+          order.leave();
           return;
         }
         fb = fbuf + (fseq & 1) * a.buf_bytes;
@@ -212,6 +219,7 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
           const bool ok = dev::mbar_wait(bar_f0, 0, a.err, a.wait_ns);
           if (__syncthreads_or(!ok)) {
             if (tid == 0) dev::drain_copies(a, bar_f0, 0, 1, bar_tile, 1, k + 1, t_issued);
+            order.leave();
             return;
           }
           fseq = 1;
@@ -256,7 +264,10 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
       }
     }
     if (row < a.rows) dev::epilogue<KT>(a, acc, row);
+    tile = next;
+    next = order.after(k, next);
   }
+  order.leave();
 }
 
 using KernelFn = void (*)(const KArgs);

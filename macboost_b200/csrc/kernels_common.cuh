@@ -330,6 +330,43 @@ static __device__ __noinline__ void drain_copies(const KArgs& a, uint32_t bar_f0
     mbar_wait(copy_bar(bar_t0, bufs, j), copy_parity(bufs, j), a.err, a.wait_ns);
 }
 
+// The tile order of a CTA-wide persistent loop.  Tile 0 of CTA b is b and
+// tile 1 is b + gridDim.x; with the launch's counter pair (KArgs::sched) the
+// later ones are claimed in row order, one tile ahead -- thread 0 claims tile
+// k + 2 during iteration k into shared slot k & 1, which the CTA reads after
+// a barrier that ends iteration k -- so CTAs on faster SMs take more tiles;
+// without counters the order is fixed (tile + k * gridDim.x).  Thread 0 of
+// every CTA counts the CTA out of `done` as it leaves (after its claims,
+// __threadfence), and the last CTA out sets both counters back to zero.
+struct TileOrder {
+  const KArgs& a;
+  uint32_t slots;  // two 8-byte shared-memory slots
+  __device__ __forceinline__ void claim_ahead(int k) const {
+    if (a.sched != nullptr && threadIdx.x == 0) {
+      const unsigned long long v =
+          2ull * gridDim.x + atomicAdd(a.sched, 1ull);
+      asm volatile("st.shared.u64 [%0], %1;" ::"r"(slots + 8u * uint32_t(k & 1)), "l"(v)
+                   : "memory");
+    }
+  }
+  // Tile after `next`, read after the barrier that ends iteration k.
+  __device__ __forceinline__ long long after(int k, long long next) const {
+    if (a.sched == nullptr) return next + gridDim.x;
+    unsigned long long v;
+    asm volatile("ld.shared.u64 %0, [%1];" : "=l"(v) : "r"(slots + 8u * uint32_t(k & 1)) : "memory");
+    return (long long)v;
+  }
+  __device__ __forceinline__ void leave() const {
+    if (a.sched != nullptr && threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(a.sched + 1, 1ull) + 1 == (unsigned long long)gridDim.x) {
+        atomicExch(a.sched, 0ull);
+        atomicExch(a.sched + 1, 0ull);
+      }
+    }
+  }
+};
+
 // The per-CTA pipeline shared by both layouts: a persistent loop over row
 // tiles (double- or single-buffered bulk staging), forest blocks (resident,
 // or streamed through two buffers), the -Inf plane fill, and the bounded-wait
@@ -359,8 +396,13 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
   }
   __syncthreads();
 
+  const TileOrder order{a, base + 64u};
   long long tile = blockIdx.x;
-  if (tile >= a.ntiles) return;  // uniform over the CTA
+  if (tile >= a.ntiles) {  // uniform over the CTA
+    order.leave();
+    return;
+  }
+  long long next = tile + gridDim.x;
 
   if (warp == 0) {
     if (a.nblocks > 0) issue_block(a, 0, fbuf, bar_f0, lane);
@@ -374,10 +416,10 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
   unsigned fseq = 0;
   const unsigned f_any = a.nblocks > 0 ? 1u : 0u;
 
-  for (int k = 0; tile < a.ntiles; tile += gridDim.x, ++k) {
+  for (int k = 0; tile < a.ntiles; ++k) {
     const int tb = (a.tile_bufs == 2) ? (k & 1) : 0;
     const uint32_t tl = tiles + uint32_t(tb) * a.tile_bytes;
-    const long long next = tile + gridDim.x;
+    order.claim_ahead(k);
     const bool ahead = bulk && a.tile_bufs == 2 && next < a.ntiles;
     if (ahead && warp == 0) {
       // buffer tb^1 held tile k-1, released by the barrier ending that iteration
@@ -394,6 +436,7 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
         if (tid == 0)
           drain_copies(a, bar_f0, fseq, streaming ? fseq + 1 : f_any, bar_tile0, a.tile_bufs, k,
                        t_issued);
+        order.leave();
         return;
       }
     } else if (a.S_stage > 0) {
@@ -437,6 +480,7 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
           if (tid == 0)
             drain_copies(a, bar_f0, fseq, fseq + (nb >= 0 ? 2u : 1u), bar_tile0, a.tile_bufs,
                          k + 1, t_issued);
+          order.leave();
           return;
         }
         fb = fbuf + (fseq & 1) * a.buf_bytes;
@@ -446,6 +490,7 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
           const bool ok = mbar_wait(bar_f0, 0, a.err, a.wait_ns);
           if (__syncthreads_or(!ok)) {
             if (tid == 0) drain_copies(a, bar_f0, 0, 1, bar_tile0, a.tile_bufs, k + 1, t_issued);
+            order.leave();
             return;
           }
           fseq = 1;
@@ -461,7 +506,10 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
       __syncwarp();
       issue_tile(a, next, tiles, bar_tile0, lane);
     }
+    tile = next;
+    next = order.after(k, next);  // claimed this iteration, before the barrier above
   }
+  order.leave();
 }
 
 // The per-warp pipeline, for a forest resident in shared memory (one block):

@@ -2,7 +2,9 @@
 
 A launch sizes its grid to one wave of resident CTAs, so on the row counts a
 test can check every CTA (and every warp of the per-warp pipeline) would take
-one row tile at most and the loop body would run once.  MACBOOST_PLAN "grid=N"
+one row tile at most and the loop body would run once.  After its first tile
+(two tiles, CTA-wide loops) each warp or CTA claims the next from the launch's
+per-stream counters ("claim=0": a fixed order), and both orders are covered.  MACBOOST_PLAN "grid=N"
 caps the CTAs of a launch; with two CTAs each one loops over many tiles, so
 these tests reach what a 10M-row launch runs: the per-warp loop's later
 chunks (mbarrier phase flips, buffer release and prefetch into the other
@@ -46,6 +48,8 @@ CASES = [
     ("cfg5", 120, 12_000, "grid=2"),                     # explicit (leaf-wise) layout
     ("cfg2", None, 30_000, "codes=1,grid=2"),            # binned codes, resident
     ("cfg4", 1000, 12_000, "codes=1,grid=2"),            # binned codes, streamed
+    ("cfg2", None, 50_000, "codes=0,claim=0,grid=2"),    # per-warp, fixed chunk order
+    ("cfg4", 300, 20_000, "codes=0,claim=0,grid=2"),     # CTA tiles, fixed tile order
 ]
 
 
