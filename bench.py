@@ -287,11 +287,16 @@ def cpu_baseline(cfg, text, X, budget_s=10.0, threads=None):
                       f"Booster.swift predictCPU)"}, raw, om
 
 
-def parity_check(O, om, raw_o, raw_gpu, out_gpu, kind):
+def parity_check(O, om, raw_o, raw_gpu, out_gpu, kind, leaf_o=None):
     """The timed step's outputs of the rows the oracle scored, against it."""
     n = raw_o.shape[0]
     raw_bitwise = bool(np.array_equal(np.ascontiguousarray(raw_gpu[:n]).view(np.uint32),
                                       np.ascontiguousarray(raw_o).view(np.uint32)))
+    if kind == 3:
+        same = bool(np.array_equal(out_gpu[:n], leaf_o))
+        return {"rows": int(n), "raw_bitwise": raw_bitwise, "leaf_indices_equal": same,
+                "against": "oracle/mbref.c (restatement of Booster.swift predictCPU, pinned to "
+                           "the reference's PyModel outputs in tests/golden)"}
     if kind == 2:
         want = O.predict_proba(raw_o if om.num_classes > 1 else raw_o[:, 0]).astype(np.float32)
     else:
@@ -416,6 +421,9 @@ def main():
                          "contributions; binned: one tree walked over binned rows per step, "
                          "as a trainer evaluates each new tree, plus bin_data")
     ap.add_argument("--trees", type=int, default=0, help="override the model's tree count")
+    ap.add_argument("--output", default="config", choices=["config", "raw", "proba", "leaf"],
+                    help="output kind: the config's (default), raw margins, predict_proba, or "
+                         "leaf indices (rows x trees int32)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -449,7 +457,9 @@ def main():
     affinity = bind_near_gpu(dev) if dist.world > 1 else None
     rows = rows_per_rank(cfg, args, dist.world)
     row_start = dist.rank * rows
-    kind = OUTPUT_KIND[cfg.output]
+    kind = OUTPUT_KIND[cfg.output] if args.output == "config" else \
+        {"raw": 1, "proba": 2, "leaf": 3}[args.output]
+    odt = np.int32 if kind == 3 else np.float32
     h = _core.load_json(text)
     _core.prepare(h, [dev])
     desc = json.loads(_core.describe(h))
@@ -459,9 +469,10 @@ def main():
     # inputs: seeded, this rank's shard, feature-major in page-locked memory
     Xh = _core.pinned_empty((cfg.features, rows))
     synth.make_data(cfg, rows=rows, row_start=row_start, layout="feature", out=Xh)
-    outh = _core.pinned_empty((rows, ocols))
+    outh = _core.pinned_empty((rows, ocols), dtype=odt)
     xd = torch.from_numpy(np.asarray(Xh)).to(f"cuda:{dev}")
-    outd = torch.empty((rows, ocols), dtype=torch.float32, device=f"cuda:{dev}")
+    outd = torch.empty((rows, ocols), dtype=torch.int32 if kind == 3 else torch.float32,
+                       device=f"cuda:{dev}")
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -535,13 +546,14 @@ def main():
     alg_bytes = rows * 4 * (S + ocols)
     # this rank's kernel: one launch per step, timed on its launching stream
     achieved = alg_bytes / (ms_local / 1e3 / args.steps) / 1e9
-    tr = traffic_lookup(cfg.name)
+    tr = traffic_lookup(cfg.name if args.output == "config" else f"{cfg.name}_{args.output}")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded model and rows; no dataset)",
-        "config": config_block(cfg, rows, args),
+        "config": dict(config_block(cfg, rows, args),
+                       **({} if args.output == "config" else {"output": args.output})),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_src,
                      "traffic": (tr["bytes_per_row"] * rows) if tr else None,
@@ -564,7 +576,12 @@ def main():
         base, raw_o, om = cpu_baseline(cfg, text, np.asarray(Xh))
         line["cpu_baseline"] = base
         from oracle import oracle as O
-        line["parity"] = parity_check(O, om, raw_o, raw_gpu, out_gpu, kind)
+        leaf_o = None
+        if kind == 3:
+            n = raw_o.shape[0]
+            _, leaf_o = O.predict_raw(om, np.ascontiguousarray(np.asarray(Xh)[:, :n]),
+                                      layout="feature", want_leaf=True)
+        line["parity"] = parity_check(O, om, raw_o, raw_gpu, out_gpu, kind, leaf_o)
         ref = reference_pymodel(cfg, text, np.asarray(Xh))
         if ref is not None:
             line["cpu_baseline_reference"] = ref

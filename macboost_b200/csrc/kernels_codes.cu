@@ -252,14 +252,14 @@ __global__ void __launch_bounds__(CodesBounds<KT, G>::kMaxThreads, 1)
           acc.add(j, t_block + g0 + j, dev::lds_f32(o[j] + kk));
         }
         if (a.out_leaf != nullptr && row < a.rows) {
+          const int t0 = t_block + g0;
+          int li[G];
 #pragma unroll
           for (int j = 0; j < G; ++j) {
-            const int t = t_block + g0 + j;
-            if (t < a.T) {
-              const uint32_t leaf = (o[j] - A[j]) / 4u - 1u - NI;
-              a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + size_t(t) * NL + leaf);
-            }
+            const uint32_t leaf = (o[j] - A[j]) / 4u - 1u - NI;
+            li[j] = t0 + j < a.T ? __ldg(a.leaf_heap + size_t(t0 + j) * NL + leaf) : 0;
           }
+          dev::store_leaf_run<G>(a.out_leaf + row * a.T + t0, li, a.T - t0);
         }
       }
     }

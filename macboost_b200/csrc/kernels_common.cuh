@@ -226,6 +226,33 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
   return uint32_t(!(fmaxf(v, c) <= t));
 }
 
+// Leaf-index output (kKindLeaf, row-major rows x T int32): this thread's row
+// gets the n <= G consecutive indices of a tree group at p with the widest
+// stores its alignment allows -- 16-byte stores when the run is a whole group
+// of a multiple of 4 trees on a 16-byte boundary (T and the group start
+// multiples of 4), so that a warp's store covers whole 32-byte sectors over
+// two instructions instead of writing 4 bytes of 32 sectors in each of G.
+template <int G>
+__device__ __forceinline__ void store_leaf_run(int* p, const int (&v)[G], int n) {
+  const uintptr_t ad = reinterpret_cast<uintptr_t>(p);
+  if (G % 4 == 0 && n == G && (ad & 15u) == 0) {
+#pragma unroll
+    for (int j = 0; j < G; j += 4)
+      asm volatile("st.global.v4.s32 [%0], {%1, %2, %3, %4};" ::"l"(p + j), "r"(v[j]),
+                   "r"(v[(j + 1) % G]), "r"(v[(j + 2) % G]), "r"(v[(j + 3) % G])
+                   : "memory");
+  } else if (G % 2 == 0 && n == G && (ad & 7u) == 0) {
+#pragma unroll
+    for (int j = 0; j < G; j += 2)
+      asm volatile("st.global.v2.s32 [%0], {%1, %2};" ::"l"(p + j), "r"(v[j]), "r"(v[(j + 1) % G])
+                   : "memory");
+  } else {
+#pragma unroll
+    for (int j = 0; j < G; ++j)
+      if (j < n) p[j] = v[j];
+  }
+}
+
 // Per-thread accumulators: KT compile-time classes, or (KT == 0) up to 128.
 template <int KT>
 struct Acc {

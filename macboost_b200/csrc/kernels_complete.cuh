@@ -101,14 +101,14 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
         acc.add(j, t_block + g0 + j, dev::lds_f32((o[j] >> 1) + k));
       }
       if (a.out_leaf != nullptr && row < a.rows) {
+        const int t0 = t_block + g0;
+        int li[G];
 #pragma unroll
         for (int j = 0; j < G; ++j) {
-          const int t = t_block + g0 + j;
-          if (t < a.T) {
-            const uint32_t leaf = (o[j] - A[j]) / 8u - NL;
-            a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + size_t(t) * NL + leaf);
-          }
+          const uint32_t leaf = (o[j] - A[j]) / 8u - NL;
+          li[j] = t0 + j < a.T ? __ldg(a.leaf_heap + size_t(t0 + j) * NL + leaf) : 0;
         }
+        dev::store_leaf_run<G>(a.out_leaf + row * a.T + t0, li, a.T - t0);
       }
     }
     };

@@ -60,12 +60,12 @@ __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
       for (int j = 0; j < G; ++j) acc.add(j, t_block + g0 + j, dev::lds_f32(o[j] + 4u));
       if (a.out_leaf != nullptr && row < a.rows) {
         const size_t rec_base = a.block_rec_base[b];
+        const int t0 = t_block + g0;
+        int li[G];
 #pragma unroll
-        for (int j = 0; j < G; ++j) {
-          const int t = t_block + g0 + j;
-          if (t < a.T)
-            a.out_leaf[row * a.T + t] = __ldg(a.leaf_heap + rec_base + (o[j] - recs) / 8u);
-        }
+        for (int j = 0; j < G; ++j)
+          li[j] = t0 + j < a.T ? __ldg(a.leaf_heap + rec_base + (o[j] - recs) / 8u) : 0;
+        dev::store_leaf_run<G>(a.out_leaf + row * a.T + t0, li, a.T - t0);
       }
     }
   };
