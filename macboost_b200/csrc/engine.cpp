@@ -624,7 +624,7 @@ bool ensure_shap_built(Engine& e, std::string& err) {
 }
 
 // Upload the path tables to `d` and pick the launch plan: the largest row
-// tile (128, 64 or 32 rows) that keeps the most rows resident per SM with
+// tile (256, 128, 64 or 32 rows) that keeps the most rows resident per SM with
 // the tile and its float64 accumulators in shared memory, else 128-row
 // tiles with both in global memory.  Called with d.mu held.
 int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
@@ -653,7 +653,7 @@ int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
   if (upload_bytes(p, s.bias.data(), s.bias.size() * 4, err)) return -1;
   d.shap_bias = static_cast<float*>(p);
   int best_rows = 0;
-  for (int R : {128, 64, 32}) {
+  for (int R : {256, 128, 64, 32}) {
     const size_t smem = shap_smem_bytes(maxu, true, S, R);
     if (smem > d.smem_optin) continue;
     int ctas = 0;

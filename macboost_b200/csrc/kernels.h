@@ -117,7 +117,7 @@ struct ShapArgs {
   int K, F, data_bins;
   float* out;
   double* scratch;              // global accumulators (gridDim x S x R) when not in shared memory
-  int R;                        // rows per CTA (= threads per CTA, <= 128)
+  int R;                        // rows per CTA (= threads per CTA, <= 256)
   long long ntiles;
   unsigned* err;                // kErrWaitTimeout when a staged block never arrived
 };

@@ -149,7 +149,7 @@ __device__ __forceinline__ void path_fixed(const PathCtx& c, const ShapUniqueRec
 }
 
 template <int MAXU, bool SMEM>
-__global__ void __launch_bounds__(128) shap_kernel(const ShapArgs a) {
+__global__ void __launch_bounds__(256, 1) shap_kernel(const ShapArgs a) {
   using L = ShapLayout<MAXU>;
   extern __shared__ __align__(128) unsigned char smem[];
   const int R = a.R;
