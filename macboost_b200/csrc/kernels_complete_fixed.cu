@@ -1,55 +1,59 @@
 // Fixed-depth builds of the complete-layout forest kernel: single-class
 // forests (regression, binary objectives) of depth 4 to 8 in groups of 8
-// trees, the common gradient-boosting shapes.  With the depth known at
-// compile time the level loop unrolls and the per-tree slot arithmetic
-// folds; on B200 the depth-6 build runs cfg2-like forests 4-8% faster than
-// the run-time-depth build.  Same semantics and layout (kernels_complete.cuh).
+// trees, the common gradient-boosting shapes, and 10-class forests of depth
+// 6 in groups of 10 (one tree per class: a 10-class softmax model).  With the
+// depth known at compile time the level loop unrolls and the per-tree slot
+// arithmetic folds; on B200 the depth-6 build runs cfg2-like forests 4-8%
+// faster than the run-time-depth build.  Same semantics and layout
+// (kernels_complete.cuh).
 #include "kernels_complete.cuh"
 
 namespace mb {
 namespace complete {
 namespace {
 
-template <int D>
+template <int KT, int G, int D>
 KernelFn fixed(bool planes, bool cat) {
   if (planes)
-    return cat ? forest_complete_kernel<1, 8, true, true, D>
-               : forest_complete_kernel<1, 8, true, false, D>;
-  return cat ? forest_complete_kernel<1, 8, false, true, D>
-             : forest_complete_kernel<1, 8, false, false, D>;
+    return cat ? forest_complete_kernel<KT, G, true, true, D>
+               : forest_complete_kernel<KT, G, true, false, D>;
+  return cat ? forest_complete_kernel<KT, G, false, true, D>
+             : forest_complete_kernel<KT, G, false, false, D>;
 }
 
-template <int D>
+template <int KT, int G, int D>
 TopKernelFn fixed_top(bool planes, bool cat) {
   if (planes)
-    return cat ? forest_complete_top_kernel<1, 8, true, true, D>
-               : forest_complete_top_kernel<1, 8, true, false, D>;
-  return cat ? forest_complete_top_kernel<1, 8, false, true, D>
-             : forest_complete_top_kernel<1, 8, false, false, D>;
+    return cat ? forest_complete_top_kernel<KT, G, true, true, D>
+               : forest_complete_top_kernel<KT, G, true, false, D>;
+  return cat ? forest_complete_top_kernel<KT, G, false, true, D>
+             : forest_complete_top_kernel<KT, G, false, false, D>;
 }
 
 }  // namespace
 
 KernelFn pick_fixed(bool planes, bool cat, int K, int G, int D) {
+  if (K == 10 && G == 10 && D == 6) return fixed<10, 10, 6>(planes, cat);
   if (K != 1 || G != 8) return nullptr;
   switch (D) {
-    case 4: return fixed<4>(planes, cat);
-    case 5: return fixed<5>(planes, cat);
-    case 6: return fixed<6>(planes, cat);
-    case 7: return fixed<7>(planes, cat);
-    case 8: return fixed<8>(planes, cat);
+    case 4: return fixed<1, 8, 4>(planes, cat);
+    case 5: return fixed<1, 8, 5>(planes, cat);
+    case 6: return fixed<1, 8, 6>(planes, cat);
+    case 7: return fixed<1, 8, 7>(planes, cat);
+    case 8: return fixed<1, 8, 8>(planes, cat);
     default: return nullptr;
   }
 }
 
 TopKernelFn pick_top_fixed(bool planes, bool cat, int K, int G, int D) {
+  if (K == 10 && G == 10 && D == 6) return fixed_top<10, 10, 6>(planes, cat);
   if (K != 1 || G != 8) return nullptr;
   switch (D) {
-    case 4: return fixed_top<4>(planes, cat);
-    case 5: return fixed_top<5>(planes, cat);
-    case 6: return fixed_top<6>(planes, cat);
-    case 7: return fixed_top<7>(planes, cat);
-    case 8: return fixed_top<8>(planes, cat);
+    case 4: return fixed_top<1, 8, 4>(planes, cat);
+    case 5: return fixed_top<1, 8, 5>(planes, cat);
+    case 6: return fixed_top<1, 8, 6>(planes, cat);
+    case 7: return fixed_top<1, 8, 7>(planes, cat);
+    case 8: return fixed_top<1, 8, 8>(planes, cat);
     default: return nullptr;
   }
 }
