@@ -205,3 +205,17 @@ def test_explicit_child_encoding_choice(lib_built):
     wide = leafwise + [synth._complete_tree(rng, 12, 10, synth.EDGES_256, 0.1)]
     d = json.loads(core.describe(core.load_json(synth.model_to_json({**base, "trees": wide}))))
     assert d["layout"] == "explicit" and d["compact_children"] is False
+
+
+def test_plan_restrictions_from_the_environment(lib_built, monkeypatch):
+    """MACBOOST_PLAN restricts the planner when a model is loaded: grid (CTAs per
+    launch), chunk (rows per host chunk) and claim=0 (fixed chunk order) are
+    recorded in the plan; without them the plan has none."""
+    core = lib_built
+    text = golden_text("cfg2_small")
+    d = json.loads(core.describe(core.load_json(text)))
+    assert "grid_cap" not in d and "chunk_rows" not in d and "claim" not in d
+    monkeypatch.setenv("MACBOOST_PLAN", "grid=3,chunk=4096,claim=0,bufs=2")
+    d = json.loads(core.describe(core.load_json(text)))
+    assert d["grid_cap"] == 3 and d["chunk_rows"] == 4096 and d["claim"] is False
+    assert d["tile_buffers"] == 2
