@@ -18,47 +18,125 @@
 namespace mb {
 namespace {
 
-// One thread per (row, tile of 8 features): the 8 bins packed into one
-// 8-byte store (a warp writes 256 contiguous bytes).
-__global__ void __launch_bounds__(256) bin_data_kernel(const float* __restrict__ x, long long rows,
+// The reference's search for a value's bin (Shaders.swift:41-76) is a binary
+// search over the feature's n = dataBins - 1 upper edges:
+//   lo = 0, hi = n; while (lo < hi) { mid = (lo + hi) / 2;
+//                                     if (v > e[mid]) lo = mid + 1; else hi = mid; }
+// Its probes form a fixed binary tree of mids that depends on n only.  That
+// tree is laid out breadth-first (node p's children at 2p + 1 and 2p + 2,
+// padded to a complete tree of depth D) with the edge each node compares, so
+// a search is D steps of p = 2p + 1 + (v > E[p]) over a table in shared
+// memory: level k of the search reads 2^k consecutive entries (one
+// shared-memory wavefront for k <= 5), where the sorted array's probes are
+// spread over the whole row of edges.  Padding nodes compare against +Inf, so
+// every non-NaN value goes left through them (v > +Inf is false) and ends at
+// the leftmost leaf below the reference search's terminal, where `res` holds
+// that terminal's bin.  The probes and comparisons are the reference's, in its
+// order, so unsorted or repeated edges bin exactly as there.
+struct BinSearch {
+  unsigned char edge[255];  // edge index compared at node p < 2^D - 1; 0xFF: padding
+  unsigned char res[256];   // bin at leaf position p - (2^D - 1)
+  int D;                    // search steps
+};
+
+// Node p of the mid tree over [lo, hi] at depth d; `D` its maximum depth.
+void build_mid_tree(BinSearch& t, unsigned lo, unsigned hi, unsigned p, int d, int D) {
+  if (lo >= hi) {
+    for (; d < D; ++d) {  // padding below a terminal: always left
+      t.edge[p] = 0xFF;
+      p = 2 * p + 1;
+    }
+    t.res[p - ((1u << D) - 1)] = static_cast<unsigned char>(lo);
+    return;
+  }
+  const unsigned mid = (lo + hi) >> 1;
+  t.edge[p] = static_cast<unsigned char>(mid);
+  build_mid_tree(t, lo, mid, 2 * p + 1, d + 1, D);
+  build_mid_tree(t, mid + 1, hi, 2 * p + 2, d + 1, D);
+}
+
+int mid_tree_depth(unsigned lo, unsigned hi) {
+  if (lo >= hi) return 0;
+  const unsigned mid = (lo + hi) >> 1;
+  return 1 + std::max(mid_tree_depth(lo, mid), mid_tree_depth(mid + 1, hi));
+}
+
+// Persistent blocks of 256 threads over one tile of 8 features (blockIdx.y):
+// the tile's search tables are staged in shared memory once per block, then
+// each thread bins its rows' 8 values -- the 8 searches interleaved, D steps
+// each -- and packs them into one 8-byte store (a warp writes 256 contiguous
+// bytes).
+template <int DT>  // search steps fixed at compile time (8: 256 bins), or 0: tree.D
+__global__ void __launch_bounds__(256, 3) bin_data_kernel(const float* __restrict__ x, long long rows,
                                                        long long cols, long long ld, int layout,
                                                        const float* __restrict__ edges,
                                                        int num_bins,
                                                        const unsigned char* __restrict__ cat,
-                                                       unsigned char* __restrict__ bins) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+                                                       unsigned char* __restrict__ bins,
+                                                       const BinSearch tree) {
+  __shared__ float E[8][256];
+  __shared__ unsigned char res[256];
   const long long g = blockIdx.y;
-  if (i >= rows) return;
   const unsigned data_bins = unsigned(num_bins) - 1u;
-  unsigned long long packed = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  const unsigned n = data_bins - 1u;  // edges per feature
+  const int D = tree.D;
+  const unsigned inner = (1u << D) - 1u;
+  for (unsigned q = threadIdx.x; q < 8u * 256u; q += blockDim.x) {
+    const unsigned k = q >> 8, p = q & 255u;
     const long long f = g * 8 + k;
-    if (f >= cols) break;
-    const float v = layout == 0 ? __ldg(x + f * ld + i) : __ldg(x + i * cols + f);
-    unsigned b;
-    if (isnan(v)) {
-      b = data_bins;  // the reserved missing bin
-    } else if (__ldg(cat + f) == 1) {
-      // clamp(int(rint(v)), 0, dataBins - 1); the int conversion saturates
-      const float r = rintf(v);
-      b = r < 0.0f ? 0u : (r > float(data_bins - 1) ? data_bins - 1 : unsigned(int(r)));
-    } else {
-      // first upper edge >= v (the reference's binary search, verbatim bounds)
-      const float* e = edges + size_t(f) * (data_bins - 1);
-      unsigned lo = 0, hi = data_bins - 1;
-      while (lo < hi) {
-        const unsigned mid = (lo + hi) >> 1;
-        if (v > __ldg(e + mid))
-          lo = mid + 1;
-        else
-          hi = mid;
-      }
-      b = lo;
-    }
-    packed |= (unsigned long long)(b & 0xFFu) << (8 * k);
+    float e = __int_as_float(0x7f800000);  // +Inf: padding, and features past cols
+    if (p < inner && f < cols && tree.edge[p] != 0xFF) e = __ldg(edges + size_t(f) * n + tree.edge[p]);
+    E[k][p] = e;
   }
-  *reinterpret_cast<unsigned long long*>(bins + (g * rows + i) * 8) = packed;
+  for (unsigned q = threadIdx.x; q < 256u; q += blockDim.x) res[q] = tree.res[q];
+  unsigned catbits = 0;  // bit k: feature g * 8 + k is categorical
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    if (g * 8 + k < cols && __ldg(cat + g * 8 + k) == 1) catbits |= 1u << k;
+  __syncthreads();
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < rows;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const long long f = g * 8 + k;
+      v[k] = f < cols ? (layout == 0 ? __ldg(x + f * ld + i) : __ldg(x + i * cols + f)) : 0.0f;
+    }
+    // p: node of each feature's search, as a byte offset into its table row
+    unsigned p[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) p[k] = 0;
+    auto step = [&]() {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float e = *reinterpret_cast<const float*>(reinterpret_cast<const char*>(E[k]) + p[k]);
+        p[k] = 2u * p[k] + (v[k] > e ? 8u : 4u);
+      }
+    };
+    if (DT > 0) {
+#pragma unroll
+      for (int s2 = 0; s2 < DT; ++s2) step();
+    } else {
+      for (int s2 = 0; s2 < D; ++s2) step();
+    }
+    unsigned long long packed = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      unsigned b;
+      if (isnan(v[k])) {
+        b = data_bins;  // the reserved missing bin
+      } else if ((catbits >> k) & 1u) {
+        // clamp(int(rint(v)), 0, dataBins - 1); the int conversion saturates
+        const float r = rintf(v[k]);
+        b = r < 0.0f ? 0u : (r > float(data_bins - 1) ? data_bins - 1 : unsigned(int(r)));
+      } else {
+        b = res[(p[k] >> 2) - inner];
+      }
+      if (g * 8 + k >= cols) b = 0;  // bytes past the last feature stay zero
+      packed |= (unsigned long long)(b & 0xFFu) << (8 * k);
+    }
+    *reinterpret_cast<unsigned long long*>(bins + (g * rows + i) * 8) = packed;
+  }
 }
 
 // Final heap index of row i in tree t, walking at most max_depth splits.
@@ -304,9 +382,26 @@ cudaError_t launch_bin_data(const float* x, long long rows, long long cols, long
                             const unsigned char* categorical, unsigned char* bins,
                             cudaStream_t stream) {
   if (rows <= 0 || cols <= 0) return cudaSuccess;
-  const dim3 grid(unsigned((rows + 255) / 256), unsigned((cols + 7) / 8));
-  bin_data_kernel<<<grid, 256, 0, stream>>>(x, rows, cols, ld, layout, edges, num_bins,
-                                            categorical, bins);
+  if (num_bins < 3 || num_bins > 256) return cudaErrorInvalidValue;
+  // the search tree of the reference's binary search over num_bins - 2 edges
+  BinSearch tree{};
+  const unsigned n = unsigned(num_bins) - 2u;
+  tree.D = mid_tree_depth(0, n);
+  build_mid_tree(tree, 0, n, 0, 0, tree.D);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = (cols + 7) / 8;
+  const long long blocks = (rows + 255) / 256;
+  // about 8 blocks per SM over all feature tiles; each block loops over rows
+  long long want = std::max<long long>(1, 8ll * sms / tiles);
+  const dim3 grid(unsigned(std::min(blocks, want)), unsigned(tiles));
+  if (tree.D == 8)
+    bin_data_kernel<8><<<grid, 256, 0, stream>>>(x, rows, cols, ld, layout, edges, num_bins,
+                                                 categorical, bins, tree);
+  else
+    bin_data_kernel<0><<<grid, 256, 0, stream>>>(x, rows, cols, ld, layout, edges, num_bins,
+                                                 categorical, bins, tree);
   return cudaGetLastError();
 }
 
