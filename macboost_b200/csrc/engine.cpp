@@ -623,10 +623,14 @@ bool ensure_shap_built(Engine& e, std::string& err) {
   return true;
 }
 
-// Upload the path tables to `d` and pick the launch plan: the largest row
-// tile (256, 128, 64 or 32 rows) that keeps the most rows resident per SM with
-// the tile and its float64 accumulators in shared memory, else 128-row
-// tiles with both in global memory.  Called with d.mu held.
+// Doubles of one scratch region of global TreeSHAP accumulators: S slots x R
+// rows per CTA of the plan's grid.
+size_t shap_region(const DeviceState& d, int S) {
+  return size_t(d.shap_grid) * size_t(std::max(S, 1)) * size_t(d.shap_R);
+}
+
+// Upload the path tables to `d` and pick the launch plan (the row tile and
+// where its float64 accumulators live, below).  Called with d.mu held.
 int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
   if (d.shap_ready) return 0;
   const ShapForest& s = e.shap;
@@ -652,8 +656,20 @@ int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
   d.shap_slot_feature = static_cast<int*>(p);
   if (upload_bytes(p, s.bias.data(), s.bias.size() * 4, err)) return -1;
   d.shap_bias = static_cast<float*>(p);
+  // Candidates: row tile and float64 accumulators in shared memory (R = 256
+  // ... 32), or, for paths of at most 8 distinct features, accumulators in a
+  // global scratch (R = 128 or 64) that the L2 holds (at most
+  // kShapScratchBytes), whose CTAs need no shared memory for them and so are
+  // limited by registers only.  The plan keeps the most rows resident per SM;
+  // shared memory wins ties.  B200, 100-feature models: depth-6 trees (cfg1,
+  // cfg4) run 19-22% faster with 3 x 128 rows per SM in global memory than
+  // with 1 x 256 in shared memory; the leaf-wise model (cfg5, paths of up to
+  // 11 features, more accumulator updates per path) runs 15% slower.
+  constexpr size_t kShapScratchBytes = size_t(64) << 20;
   int best_rows = 0;
+  const int force_global = plan_shap_global_from_env();  // MACBOOST_PLAN "shapglobal=N"
   for (int R : {256, 128, 64, 32}) {
+    if (force_global > 0) break;
     const size_t smem = shap_smem_bytes(maxu, true, S, R);
     if (smem > d.smem_optin) continue;
     int ctas = 0;
@@ -666,8 +682,25 @@ int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
       d.shap_in_smem = true;
     }
   }
+  for (int R : {128, 64}) {
+    if (maxu > 8 && force_global == 0) break;
+    const size_t smem = shap_smem_bytes(maxu, false, S, R);
+    int ctas = 0;
+    MB_CUDA(shap_occupancy(maxu, false, R, smem, &ctas), "occupancy query (SHAP)");
+    const size_t per_cta = size_t(std::max(S, 1)) * size_t(R) * sizeof(double);
+    const int fit = int(std::min<size_t>(kShapScratchBytes / (per_cta * size_t(d.num_sms)), 64));
+    ctas = std::min(ctas, force_global > 0 ? force_global : fit);
+    if (ctas >= 1 && ctas * R > best_rows) {
+      best_rows = ctas * R;
+      d.shap_R = R;
+      d.shap_smem = smem;
+      d.shap_grid = ctas * d.num_sms;
+      d.shap_in_smem = false;
+    }
+  }
   if (best_rows == 0) {
-    const int R = 128;
+    // very wide models: one 64-row CTA per SM with its accumulators in global memory
+    const int R = 64;
     const size_t smem = shap_smem_bytes(maxu, false, S, R);
     int ctas = 0;
     MB_CUDA(shap_occupancy(maxu, false, R, smem, &ctas), "occupancy query (SHAP)");
@@ -677,20 +710,26 @@ int prepare_shap(Engine& e, DeviceState& d, std::string& err) {
     }
     d.shap_R = R;
     d.shap_smem = smem;
-    d.shap_grid = std::min(ctas, 2) * d.num_sms;  // bounds the scratch: S x 1 KiB per CTA
+    d.shap_grid = d.num_sms;
     d.shap_in_smem = false;
-    MB_CUDA(cudaMalloc(reinterpret_cast<void**>(&d.shap_scratch),
-                       size_t(d.shap_grid) * size_t(S) * R * sizeof(double)),
-            "cudaMalloc (SHAP accumulators)");
   }
+  // two regions: the double-buffered chunks of a host-memory call run on two
+  // streams at once, each with its own (the device entry point uses region 0
+  // and waits for its kernel)
+  if (!d.shap_in_smem)
+    MB_CUDA(cudaMalloc(reinterpret_cast<void**>(&d.shap_scratch),
+                       2 * shap_region(d, S) * sizeof(double)),
+            "cudaMalloc (SHAP accumulators)");
   d.shap_ready = true;
   return 0;
 }
 
 // Enqueue the contributions kernel over `rows` rows of feature-major x
-// (stride ld; slot_map null: x holds the staged slots in order).
+// (stride ld; slot_map null: x holds the staged slots in order), with global
+// accumulators (when the plan has them) in scratch region `region` (0 or 1).
 int launch_shap_on(Engine& e, DeviceState& d, const float* x, int64_t rows, int64_t ld,
-                   const int* slot_map, float* out, cudaStream_t st, std::string& err) {
+                   const int* slot_map, float* out, cudaStream_t st, std::string& err,
+                   int region = 0) {
   const ShapForest& s = e.shap;
   ShapArgs a{};
   a.x = x;
@@ -712,7 +751,7 @@ int launch_shap_on(Engine& e, DeviceState& d, const float* x, int64_t rows, int6
   a.F = int(e.model.num_features);
   a.data_bins = e.model.num_bins - 1;
   a.out = out;
-  a.scratch = d.shap_scratch;
+  a.scratch = d.shap_scratch ? d.shap_scratch + size_t(region) * shap_region(d, a.S) : nullptr;
   a.R = d.shap_R;
   a.ntiles = (rows + a.R - 1) / a.R;
   int64_t grid = std::min<int64_t>(d.shap_grid, a.ntiles);
@@ -795,7 +834,7 @@ int run_contrib_slice(Engine& e, DeviceState& d, const float* x, int64_t rows, i
       slot_map = d.shap_slot_feature;
     }
     if (launch_shap_on(e, d, d.xbuf[p], nr, ldc, slot_map, static_cast<float*>(d.obuf[p]), st,
-                       err))
+                       err, p))
       return -1;
     if (prev_r0 >= 0 && drain(prev_p, prev_r0, prev_n)) return -1;
     prev_r0 = r0;

@@ -46,7 +46,8 @@ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // tuning and tests: MACBOOST_PLAN="G=8,R=256,bufs=2,planes=0,grid=2,chunk=4096,claim=0"
 // (any subset; 0 = free).
 struct PlanOverride {
-  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0, claim = -1;
+  int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0, claim = -1,
+      shapglobal = 0;
   long chunk = 0;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
@@ -66,6 +67,7 @@ struct PlanOverride {
       else if (key == "top") top = int(v);
       else if (key == "grid") grid = int(v);
       else if (key == "claim") claim = int(v);
+      else if (key == "shapglobal") shapglobal = int(v);
       else if (key == "chunk") chunk = v;
       p = end;
       while (*p == ',' || *p == ' ') ++p;
@@ -196,6 +198,7 @@ bool make_blocks(int ngroups, int G, size_t max_block,
 static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int force_planes);
 
 int plan_grid_cap_from_env() { return std::max(0, PlanOverride().grid); }
+int plan_shap_global_from_env() { return std::max(0, PlanOverride().shapglobal); }
 
 bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_planes) {
   const PlanOverride ov;

@@ -174,6 +174,9 @@ bool flatten_codes(const Model& m, FlatForest& out, std::string& why, int force_
 // The "grid" restriction of MACBOOST_PLAN (0 when unset), for launchers that
 // have no forest plan (the binned-data kernels).
 int plan_grid_cap_from_env();
+// The "shapglobal" restriction (0 when unset): TreeSHAP accumulators in global
+// memory, at most that many 128-row CTAs per SM.
+int plan_shap_global_from_env();
 
 // Human-readable JSON description of a flattened forest.
 std::string describe_forest(const FlatForest& f);

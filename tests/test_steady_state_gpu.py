@@ -106,17 +106,28 @@ def test_host_chunks_vs_oracle(gpu, oracle_built, monkeypatch, plan):
                        f"{plan} devices={devs}")
 
 
-def test_contrib_persistent_loop(gpu, oracle_built, monkeypatch):
-    """TreeSHAP's persistent CTAs over many row tiles and host chunks."""
+@pytest.mark.parametrize("cfg,plan", [
+    ("cfg2", "grid=2,chunk=1024"),                 # accumulators in shared memory
+    ("cfg1", "grid=2,chunk=1024"),                 # 100 features: accumulators in global memory
+    ("cfg2", "grid=3,chunk=1024,shapglobal=2"),    # global accumulators forced
+    ("cfg1", "chunk=1000"),                        # two streams' chunks overlapping, full grid
+])
+def test_contrib_persistent_loop(gpu, oracle_built, monkeypatch, cfg, plan):
+    """TreeSHAP's persistent CTAs over many row tiles and host chunks (the
+    chunks of the two streams use separate global accumulator regions)."""
     from test_shap_gpu import assert_contrib_close, covered
     core = gpu
-    monkeypatch.setenv("MACBOOST_PLAN", "grid=2,chunk=1024")
-    text, om = covered("cfg2", 40)
+    monkeypatch.setenv("MACBOOST_PLAN", plan)
+    text, om = covered(cfg, 40)
     h = core.load_json(text)
-    X = synth.make_data("cfg2", rows=3000, row_start=77_777, layout="row")
+    X = synth.make_data(cfg, rows=3000, row_start=77_777, layout="row")
     want = O.predict_contrib(om, X)
     got = core.predict_contrib_ex(h, X, layout="row", devices=[0])
-    assert assert_contrib_close(got, want, "contrib grid=2") > 0.95
+    assert assert_contrib_close(got, want, f"contrib {cfg} {plan}") > 0.95
+    # the device entry point on the same handle (accumulator region 0, waits)
+    Xf = np.ascontiguousarray(X.T)
+    got_d = core.predict_contrib_ex(h, Xf, layout="feature", devices=[0])
+    assert assert_contrib_close(got_d, want, f"contrib {cfg} {plan} feature-major") > 0.95
 
 
 def test_binned_walk_persistent_loop(gpu, oracle_built, monkeypatch):
