@@ -66,6 +66,7 @@ struct DeviceState {
   double* shap_scratch = nullptr;       // accumulators when they do not fit in shared memory
   int shap_R = 0;
   bool shap_in_smem = true;
+  bool shap_dense = false;              // the 128-register build (global accumulators)
   size_t shap_smem = 0;
   int shap_grid = 0;
   std::mutex mu;                        // one predict at a time per (model, device)

@@ -47,7 +47,7 @@ inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // (any subset; 0 = free).
 struct PlanOverride {
   int G = 0, R = 0, bufs = 0, planes = -1, codes = -1, top = -1, grid = 0, claim = -1,
-      shapglobal = 0;
+      shapglobal = 0, shapdense = -1;
   long chunk = 0;
   PlanOverride() {
     const char* s = std::getenv("MACBOOST_PLAN");
@@ -68,6 +68,7 @@ struct PlanOverride {
       else if (key == "grid") grid = int(v);
       else if (key == "claim") claim = int(v);
       else if (key == "shapglobal") shapglobal = int(v);
+      else if (key == "shapdense") shapdense = int(v);
       else if (key == "chunk") chunk = v;
       p = end;
       while (*p == ',' || *p == ' ') ++p;
@@ -199,6 +200,7 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
 
 int plan_grid_cap_from_env() { return std::max(0, PlanOverride().grid); }
 int plan_shap_global_from_env() { return std::max(0, PlanOverride().shapglobal); }
+int plan_shap_dense_from_env() { return PlanOverride().shapdense; }
 
 bool flatten_forest(const Model& m, FlatForest& f, std::string& err, int force_planes) {
   const PlanOverride ov;

@@ -177,6 +177,9 @@ int plan_grid_cap_from_env();
 // The "shapglobal" restriction (0 when unset): TreeSHAP accumulators in global
 // memory, at most that many 128-row CTAs per SM.
 int plan_shap_global_from_env();
+// The "shapdense" restriction: 0 keeps TreeSHAP off its 128-register build
+// (-1 when unset).
+int plan_shap_dense_from_env();
 
 // Human-readable JSON description of a flattened forest.
 std::string describe_forest(const FlatForest& f);

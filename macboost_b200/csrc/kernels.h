@@ -124,9 +124,12 @@ struct ShapArgs {
 // Dynamic shared memory of the contributions kernel (maxu: longest path in
 // distinct features; smem_variant: row tile and accumulators in shared memory).
 size_t shap_smem_bytes(int maxu, bool smem_variant, int S, int R);
-cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas);
+// dense: the build with launch bounds (128, 4), global accumulators and paths
+// of at most 12 distinct features only
+cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas,
+                           bool dense = false);
 cudaError_t launch_shap(const ShapArgs& a, int maxu, bool smem_variant, size_t smem, int grid,
-                        cudaStream_t stream);
+                        cudaStream_t stream, bool dense = false);
 // Binned data (kernels_binned.cu).  Tiled bins as MacBoost's trainer keeps
 // them: bins[(f / 8) * n * 8 + i * 8 + f % 8] for n rows.
 cudaError_t launch_bin_data(const float* x, long long rows, long long cols, long long ld,

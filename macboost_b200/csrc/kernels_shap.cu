@@ -148,8 +148,11 @@ __device__ __forceinline__ void path_fixed(const PathCtx& c, const ShapUniqueRec
   }
 }
 
-template <int MAXU, bool SMEM>
-__global__ void __launch_bounds__(256, 1) shap_kernel(const ShapArgs a) {
+// MAXT, MINB: launch bounds.  The dense build (128 threads, 4 CTAs per SM)
+// caps registers at 128 so that four 128-row CTAs fit an SM when the
+// accumulators live in global memory.
+template <int MAXU, bool SMEM, int MAXT = 256, int MINB = 1>
+__global__ void __launch_bounds__(MAXT, MINB) shap_kernel(const ShapArgs a) {
   using L = ShapLayout<MAXU>;
   extern __shared__ __align__(128) unsigned char smem[];
   const int R = a.R;
@@ -313,7 +316,8 @@ __global__ void __launch_bounds__(256, 1) shap_kernel(const ShapArgs a) {
 
 using ShapKernel = void (*)(const ShapArgs);
 
-ShapKernel pick(int maxu, bool smem_variant) {
+ShapKernel pick(int maxu, bool smem_variant, bool dense) {
+  if (dense && maxu <= 12 && !smem_variant) return shap_kernel<12, false, 128, 4>;
   if (maxu <= 12) return smem_variant ? shap_kernel<12, true> : shap_kernel<12, false>;
   return smem_variant ? shap_kernel<kShapMaxUnique, true> : shap_kernel<kShapMaxUnique, false>;
 }
@@ -325,17 +329,18 @@ size_t shap_smem_bytes(int maxu, bool smem_variant, int S, int R) {
   return fixed + (smem_variant ? size_t(S) * R * 8 : 0);
 }
 
-cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas) {
-  ShapKernel k = pick(maxu, smem_variant);
+cudaError_t shap_occupancy(int maxu, bool smem_variant, int R, size_t smem, int* ctas,
+                           bool dense) {
+  ShapKernel k = pick(maxu, smem_variant, dense);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, k, R, smem);
 }
 
 cudaError_t launch_shap(const ShapArgs& a, int maxu, bool smem_variant, size_t smem, int grid,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, bool dense) {
   if (a.rows <= 0) return cudaSuccess;
-  ShapKernel k = pick(maxu, smem_variant);
+  ShapKernel k = pick(maxu, smem_variant, dense);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
   k<<<grid, a.R, smem, stream>>>(a);

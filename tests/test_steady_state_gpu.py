@@ -111,6 +111,8 @@ def test_host_chunks_vs_oracle(gpu, oracle_built, monkeypatch, plan):
     ("cfg1", "grid=2,chunk=1024"),                 # 100 features: accumulators in global memory
     ("cfg2", "grid=3,chunk=1024,shapglobal=2"),    # global accumulators forced
     ("cfg1", "chunk=1000"),                        # two streams' chunks overlapping, full grid
+    ("cfg1", "grid=3,shapdense=0"),                # the 154-register global build
+    ("cfg4", "grid=3,chunk=1024,shapdense=1"),     # the 128-register build, 10 classes
 ])
 def test_contrib_persistent_loop(gpu, oracle_built, monkeypatch, cfg, plan):
     """TreeSHAP's persistent CTAs over many row tiles and host chunks (the
