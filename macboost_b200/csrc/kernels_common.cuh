@@ -196,18 +196,31 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
                                           int data_bins) {
   const uint32_t addr = rowbase + ((PLANES && !CAT) ? r.x : (r.x & kRecSlotMask));
   const float v = lds_f32(addr);
-  if (CAT && (r.x & kRecCategorical)) {
-    int code = data_bins;                  // non-finite / out of range -> missing bin
-    if (isfinite(v)) {
-      const float q = rintf(v);            // round half to even
-      if (q >= 0.0f && q < float(data_bins)) code = int(q);
+  if constexpr (CAT) {
+    // Both decisions, then a select: the 32 rows of a warp sit at categorical
+    // and numeric nodes alike below the root, and a branch would run both
+    // sides anyway.  Numeric: as below (the record's low bits are the
+    // default-left bit and zeros only for numeric records; the categorical
+    // result replaces the other).  Categorical: code = rint(v) (half to even)
+    // when 0 <= rint(v) < dataBins, else dataBins (NaN and infinities fail both
+    // comparisons), then the node's mask bit at the code.
+    const float t = __uint_as_float(r.y);
+    uint32_t right_num;
+    if (PLANES || NONAN) {
+      right_num = uint32_t(!(v <= t));
+    } else {
+      const float c = __uint_as_float(__funnelshift_l(0u, 0x7FC00000u, r.x));
+      right_num = uint32_t(!(fmaxf(v, c) <= t));
     }
+    const float q = rintf(v);
+    const uint32_t code =
+        (q >= 0.0f && q < float(data_bins)) ? uint32_t(q) : uint32_t(data_bins);
     uint32_t left;
-    if (r.x & kRecFullMask)
-      left = (__ldg(masks + size_t(r.y) * 8 + (code >> 5)) >> (code & 31)) & 1u;
+    if (r.x & kRecFullMask)  // a mask that bits 32..dataBins do not share: in memory
+      left = (__ldg(masks + size_t(r.y) * 8 + (code >> 5)) >> (code & 31u)) & 1u;
     else
-      left = code < 32 ? (r.y >> code) & 1u : (r.x & kRecDefaultLeft);
-    return left ^ 1u;
+      left = code < 32u ? (r.y >> (code & 31u)) & 1u : (r.x & kRecDefaultLeft);
+    return (r.x & kRecCategorical) ? (left ^ 1u) : right_num;
   }
   const float t = __uint_as_float(r.y);
   // NONAN: the row tile holds no NaN, so the default direction cannot matter
