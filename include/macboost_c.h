@@ -20,6 +20,9 @@
  * machine without such a GPU the predict entry points fail with a message.
  * Handles may be used from several threads; predicts on one handle and one
  * GPU are serialised.
+ * A kernel that waits longer than MACBOOST_WAIT_LIMIT_US microseconds (default
+ * 2,000,000) for a shared-memory transfer gives up; the call (or the next
+ * macboost_check_device) then fails with "gave up waiting".
  */
 #ifndef MACBOOST_C_H
 #define MACBOOST_C_H
@@ -129,7 +132,10 @@ int32_t macboost_predict_ex(void *handle, const float *x, int64_t rows, int64_t 
  * work completes.  Feature-major x_dev is x_dev[f * ld + i] (ld >= rows);
  * row-major x_dev is x_dev[i * cols + f] (ld ignored; this form waits for
  * completion).  16-byte aligned x_dev with ld % 4 == 0 enables bulk staging.
- * Kernel-side faults are reported by macboost_check_device. */
+ * Kernel-side faults are reported by macboost_check_device.  Calls on different
+ * streams may run at once: the kernel's row-chunk counters are kept per
+ * (handle, device, stream), so launches that overlap must come from different
+ * streams (the per-thread default stream takes a fixed chunk order instead). */
 int32_t macboost_predict_device(void *handle, int32_t device, const float *x_dev, int64_t rows,
                                 int64_t cols, int64_t ld, int32_t layout, int32_t kind,
                                 void *out_dev, void *stream, char **err);
