@@ -121,6 +121,9 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.conv_src = d.conv_src;
   a.conv_dst = d.conv_dst;
   a.n_conv = int(f.conv_src.size());
+  a.code_src = d.code_src;
+  a.code_dst = d.code_dst;
+  a.n_codes = int(f.code_src.size());
   a.K = f.K;
   a.G = f.G;
   a.T = f.T;
@@ -187,6 +190,7 @@ DeviceState::~DeviceState() {
   for (auto* p : {static_cast<void*>(blob), static_cast<void*>(block_off),
                   static_cast<void*>(block_rec_base), static_cast<void*>(stage_feature),
                   static_cast<void*>(conv_src), static_cast<void*>(conv_dst),
+                  static_cast<void*>(code_src), static_cast<void*>(code_dst),
                   static_cast<void*>(search), static_cast<void*>(bin_plan),
                   static_cast<void*>(masks), static_cast<void*>(leaf_heap),
                   static_cast<void*>(base), static_cast<void*>(err), static_cast<void*>(sched),
@@ -294,10 +298,13 @@ DeviceState* engine_prepare(Engine& e, int device, std::string& err) {
   std::vector<int> slots(e.flat.stage_feature.begin(), e.flat.stage_feature.end());
   std::vector<int> csrc(e.flat.conv_src.begin(), e.flat.conv_src.end());
   std::vector<int> cdst(e.flat.conv_dst.begin(), e.flat.conv_dst.end());
+  std::vector<int> ksrc(e.flat.code_src.begin(), e.flat.code_src.end());
+  std::vector<int> kdst(e.flat.code_dst.begin(), e.flat.code_dst.end());
   std::vector<int> heap(e.flat.leaf_heap.begin(), e.flat.leaf_heap.end());
   if (upload(d->blob, e.flat.blob, err) || upload(d->block_off, boff, err) ||
       upload(d->block_rec_base, rec_base, err) || upload(d->stage_feature, slots, err) ||
       upload(d->conv_src, csrc, err) || upload(d->conv_dst, cdst, err) ||
+      upload(d->code_src, ksrc, err) || upload(d->code_dst, kdst, err) ||
       upload(d->search, search, err) || upload(d->bin_plan, bin_plan, err) ||
       upload(d->masks, masks, err) || upload(d->leaf_heap, heap, err) ||
       upload(d->base, base, err))

@@ -31,6 +31,8 @@ struct DeviceState {
   int* stage_feature = nullptr;        // staged slot -> feature
   int* conv_src = nullptr;             // -Inf plane fills
   int* conv_dst = nullptr;
+  int* code_src = nullptr;             // category-code fills
+  int* code_dst = nullptr;
   float* search = nullptr;             // binned codes: threshold search tables
   int* bin_plan = nullptr;             // binned codes: per staged slot conversions
   unsigned* masks = nullptr;

@@ -81,16 +81,21 @@ struct SlotPlan {
   std::vector<int32_t> raw_slot;        // feature -> staged slot (or -1)
   std::vector<int32_t> left_slot;       // feature -> -Inf slot (planes) (or -1)
   std::vector<int32_t> conv_src, conv_dst;
+  std::vector<int32_t> code_slot;       // feature -> slot of its category codes (or -1)
+  std::vector<int32_t> code_src, code_dst;
   int S_stage = 0, S_total = 0;
 };
 
 // Which features are read, and by which kinds of split.
 void scan_usage(const Model& m, std::vector<char>& used, std::vector<char>& need_raw,
-                std::vector<char>& need_left) {
+                std::vector<char>& need_left, std::vector<char>& numeric,
+                std::vector<char>& categorical) {
   const size_t F = size_t(m.num_features);
   used.assign(F, 0);
   need_raw.assign(F, 0);
   need_left.assign(F, 0);
+  numeric.assign(F, 0);
+  categorical.assign(F, 0);
   for (const Tree& t : m.trees) {
     std::vector<int64_t> st{0};
     while (!st.empty()) {
@@ -100,12 +105,16 @@ void scan_usage(const Model& m, std::vector<char>& used, std::vector<char>& need
       if (f < 0) continue;
       used[size_t(f)] = 1;
       const uint32_t fl = t.flags[size_t(o)];
-      if ((fl & kFlagCategorical) && !t.cat_mask.empty())
+      if ((fl & kFlagCategorical) && !t.cat_mask.empty()) {
         need_raw[size_t(f)] = 1;  // categorical code from the raw value
-      else if (fl & kFlagDefaultLeft)
-        need_left[size_t(f)] = 1;
-      else
-        need_raw[size_t(f)] = 1;
+        categorical[size_t(f)] = 1;
+      } else {
+        numeric[size_t(f)] = 1;
+        if (fl & kFlagDefaultLeft)
+          need_left[size_t(f)] = 1;
+        else
+          need_raw[size_t(f)] = 1;
+      }
       st.push_back(2 * o + 1);
       st.push_back(2 * o + 2);
     }
@@ -113,8 +122,8 @@ void scan_usage(const Model& m, std::vector<char>& used, std::vector<char>& need
 }
 
 SlotPlan make_slots(const Model& m, bool planes) {
-  std::vector<char> used, need_raw, need_left;
-  scan_usage(m, used, need_raw, need_left);
+  std::vector<char> used, need_raw, need_left, numeric, categorical;
+  scan_usage(m, used, need_raw, need_left, numeric, categorical);
   SlotPlan p;
   const size_t F = size_t(m.num_features);
   p.raw_slot.assign(F, -1);
@@ -126,6 +135,16 @@ SlotPlan make_slots(const Model& m, bool planes) {
     }
   p.S_stage = int(p.stage_feature.size());
   p.S_total = p.S_stage;
+  // Category codes: a feature that only categorical splits read has its staged
+  // values replaced by their codes; one that numeric splits read too gets a
+  // slot of codes beside its values.
+  p.code_slot.assign(F, -1);
+  for (size_t f = 0; f < F; ++f) {
+    if (!used[f] || !categorical[f]) continue;
+    p.code_slot[f] = numeric[f] ? p.S_total++ : p.raw_slot[f];
+    p.code_src.push_back(p.raw_slot[f]);
+    p.code_dst.push_back(p.code_slot[f]);
+  }
   if (planes) {
     for (size_t f = 0; f < F; ++f) {
       if (!used[f] || !need_left[f]) continue;
@@ -150,7 +169,7 @@ uint2_like encode_split(const Tree& t, int64_t o, const SlotPlan& sp, bool plane
   const uint32_t fl = t.flags[size_t(o)];
   const uint32_t row_bytes = uint32_t(R) * 4u;
   if ((fl & kFlagCategorical) && !t.cat_mask.empty()) {
-    const uint32_t off = uint32_t(sp.raw_slot[size_t(f)]) * row_bytes;
+    const uint32_t off = uint32_t(sp.code_slot[size_t(f)]) * row_bytes;  // the codes
     const uint32_t* w = &t.cat_mask[size_t(o) * 8];
     bool uniform = true;
     uint32_t hb = 0;
@@ -427,6 +446,8 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
   f.stage_feature = sp.stage_feature;
   f.conv_src = sp.conv_src;
   f.conv_dst = sp.conv_dst;
+  f.code_src = sp.code_src;
+  f.code_dst = sp.code_dst;
   const int R = f.plan.R;
   const int nb = int(blocks.size());
   f.Tpad = nb ? blocks.back().first + blocks.back().second : 0;

@@ -123,10 +123,15 @@ struct FlatForest {
   int G = 8;              // tree group size
   int K = 1;
   int S_stage = 0;        // staged slots (one per used feature)
-  int S_total = 0;        // staged + -Inf slots
+  int S_total = 0;        // staged + -Inf slots + category-code slots beside values
   std::vector<int32_t> stage_feature;  // [S_stage] model feature of each staged slot
   std::vector<int32_t> conv_src;       // -Inf slot fills: source slot ...
   std::vector<int32_t> conv_dst;       // ... and destination slot (may be equal)
+  // category codes: the kernel writes each staged value of slot code_src[i]
+  // as its category code (integer bits) into slot code_dst[i] (the same slot
+  // when only categorical splits read the feature), and categorical records
+  // address the code slots
+  std::vector<int32_t> code_src, code_dst;
   LaunchPlan plan;
   std::vector<uint8_t> blob;           // all blocks
   std::vector<uint64_t> block_off;     // [nblocks + 1] byte offsets in blob

@@ -30,6 +30,9 @@ struct KArgs {
   const int* conv_src;             // [n_conv] -Inf slot fills (src slot -> dst slot)
   const int* conv_dst;
   int S_stage, n_conv;
+  const int* code_src;             // [n_codes] category-code fills (value slot -> code slot)
+  const int* code_dst;
+  int n_codes;
   // Forest (device copy of FlatForest).
   const unsigned char* blob;
   const unsigned long long* block_off;  // [nblocks + 1]

@@ -172,6 +172,41 @@ __device__ __forceinline__ void fill_left_planes_warp(const KArgs& a, uint32_t s
   __syncwarp();
 }
 
+// Category code of a staged value: rint(v) (half to even) when 0 <= rint(v) <
+// dataBins, else dataBins, the missing bin (NaN and infinities fail both
+// comparisons); Booster.swift:2052-2058, _pyinfer.py:80-86.
+__device__ __forceinline__ uint32_t category_code(float v, int data_bins) {
+  const float q = rintf(v);
+  return (q >= 0.0f && q < float(data_bins)) ? uint32_t(q) : uint32_t(data_bins);
+}
+
+// Each thread, its own row: write the category codes of the code slots (as
+// integer bits), from the value slots.
+__device__ __forceinline__ void fill_codes(const KArgs& a, uint32_t rowbase) {
+  for (int i = 0; i < a.n_codes; ++i) {
+    const uint32_t src = uint32_t(__ldg(a.code_src + i)) * uint32_t(a.R) * 4u;
+    const uint32_t dst = uint32_t(__ldg(a.code_dst + i)) * uint32_t(a.R) * 4u;
+    sts_f32(rowbase + dst, __uint_as_float(category_code(lds_f32(rowbase + src), a.data_bins)));
+  }
+}
+
+// The same for a warp's 32-row slice, eight lanes per slot with 16-byte
+// accesses; the warp syncs after (lanes write other lanes' rows).
+__device__ __forceinline__ void fill_codes_warp(const KArgs& a, uint32_t slice, int lane) {
+  const uint32_t part = uint32_t(lane & 7) * 16u;
+  for (int i = lane >> 3; i < a.n_codes; i += 4) {
+    const uint32_t src = uint32_t(__ldg(a.code_src + i)) * uint32_t(a.R) * 4u;
+    const uint32_t dst = uint32_t(__ldg(a.code_dst + i)) * uint32_t(a.R) * 4u;
+    float4 v = lds_v4f(slice + src + part);
+    v.x = __uint_as_float(category_code(v.x, a.data_bins));
+    v.y = __uint_as_float(category_code(v.y, a.data_bins));
+    v.z = __uint_as_float(category_code(v.z, a.data_bins));
+    v.w = __uint_as_float(category_code(v.w, a.data_bins));
+    sts_v4f(slice + dst + part, v);
+  }
+  __syncwarp();
+}
+
 // Warp 0: stage forest block b (16 KB bulk copies spread over the lanes).
 __device__ __forceinline__ void issue_block(const KArgs& a, int b, uint32_t dst, uint32_t bar,
                                             int lane) {
@@ -201,9 +236,9 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
     // and numeric nodes alike below the root, and a branch would run both
     // sides anyway.  Numeric: as below (the record's low bits are the
     // default-left bit and zeros only for numeric records; the categorical
-    // result replaces the other).  Categorical: code = rint(v) (half to even)
-    // when 0 <= rint(v) < dataBins, else dataBins (NaN and infinities fail both
-    // comparisons), then the node's mask bit at the code.
+    // result replaces the other).  Categorical: categorical records address a
+    // slot of category codes (fill_codes wrote them when the tile landed), and
+    // the node's mask bit at the code decides.
     const float t = __uint_as_float(r.y);
     uint32_t right_num;
     if (PLANES || NONAN) {
@@ -212,9 +247,7 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
       const float c = __uint_as_float(__funnelshift_l(0u, 0x7FC00000u, r.x));
       right_num = uint32_t(!(fmaxf(v, c) <= t));
     }
-    const float q = rintf(v);
-    const uint32_t code =
-        (q >= 0.0f && q < float(data_bins)) ? uint32_t(q) : uint32_t(data_bins);
+    const uint32_t code = __float_as_uint(v);
     uint32_t left;
     if (r.x & kRecFullMask)  // a mask that bits 32..dataBins do not share: in memory
       left = (__ldg(masks + size_t(r.y) * 8 + (code >> 5)) >> (code & 31u)) & 1u;
@@ -500,6 +533,9 @@ __device__ __forceinline__ void run_tiles(const KArgs& a, unsigned char* smem, S
       }
       clean = !__syncthreads_or(nan);
     }
+    // own row only, after the scan above has read every row: the codes may
+    // replace values in place
+    fill_codes(a, rowbase);
     Acc<KT> acc;
     acc.init(a.base, a.K);
     for (int b = 0; b < a.nblocks; ++b) {
@@ -697,6 +733,7 @@ __device__ __forceinline__ void run_warps(const KArgs& a, unsigned char* smem, S
       forest_ready = true;
     }
     fill_left_planes_warp(a, tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u, lane);
+    fill_codes_warp(a, tiles + uint32_t(buf) * a.tile_bytes + uint32_t(warp) * 128u, lane);
     // CHECK_NAN: the warp scans its 32 rows of every staged slot (16-byte
     // loads, 8 lanes per slot); rows past the end of the input hold stale
     // values, which can only clear `clean`.
