@@ -68,7 +68,7 @@ int ensure(void*& buf, size_t& cap, size_t bytes, std::string& err) {
 }
 
 // Kernel family: 0 complete, 1 explicit, 2 complete with binned codes.
-int layout_code(const FlatForest& f) { return f.codes ? 2 : int(f.layout); }
+int layout_code(const FlatForest& f) { return f.codes ? 2 : (f.payload ? 3 : int(f.layout)); }
 
 // Device-wait settings, read at each launch: MACBOOST_WAIT_LIMIT_US bounds
 // every mbarrier wait of the forest kernels (2 s when unset or invalid), and

@@ -74,6 +74,13 @@ constexpr uint32_t kRecCategorical = 2u;
 constexpr uint32_t kRecFullMask = 4u;
 constexpr uint32_t kRecSlotMask = 0x3FF80u;   // bits 7..17
 constexpr int kRecChildShift = 18;
+// Complete layout without planes or categorical splits (FlatForest::payload):
+// a numeric record's slot word, as a float, is the operand of the walk's
+// fmax(v, c) -- a NaN for default-right nodes (fmax keeps v, and the unordered
+// compare sends NaN right), a finite value at or below -2^127 for default-left
+// ones (fmax turns NaN into it) -- with the slot offset in bits 7..17.
+constexpr uint32_t kRecPayloadLeft = 0xFF000000u;
+constexpr uint32_t kRecPayloadRight = 0xFF800001u;
 constexpr uint32_t kMaxChildDelta = 16383u;
 constexpr uint32_t kMaxCompactDelta = 2047u;  // 8 x distance still fits bits 18-31
 
@@ -155,6 +162,9 @@ struct FlatForest {
   // rank among the forest's distinct thresholds of that feature, stored as
   // code_bytes-wide codes; node records are 4 bytes.
   bool codes = false;
+  // Complete layout: numeric records hold kRecPayloadLeft/Right (launched as
+  // layout 3).
+  bool payload = false;
   int code_bytes = 1;                  // 1 (u8) or 2 (u16)
   int S_code = 0;                      // code slots in the tile
   uint32_t code_tile_bytes = 0;        // bytes of the code tile (after the raw tile)

@@ -30,9 +30,11 @@ __global__ void __launch_bounds__(256) transpose_kernel(const float* __restrict_
 cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,
                           int grid, cudaStream_t stream, int code_bytes, const TopRecords* top) {
   if (layout == 2) return launch_codes(code_bytes, cat, a, smem, grid, stream, nullptr);
-  if (layout == 0 && top) return launch_complete_top(planes, cat, a, *top, smem, grid, stream, nullptr);
-  return layout == 0 ? launch_complete(planes, cat, a, smem, grid, stream, nullptr)
-                     : launch_explicit(planes, cat, a, smem, grid, stream, nullptr);
+  const bool pay = layout == 3;
+  if ((layout == 0 || pay) && top)
+    return launch_complete_top(planes, cat, pay, a, *top, smem, grid, stream, nullptr);
+  return (layout == 0 || pay) ? launch_complete(planes, cat, pay, a, smem, grid, stream, nullptr)
+                              : launch_explicit(planes, cat, a, smem, grid, stream, nullptr);
 }
 
 cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, int R,
@@ -42,12 +44,13 @@ cudaError_t forest_occupancy(int layout, bool planes, bool cat, int K, int G, in
   a.G = G;
   a.R = R;
   if (layout == 2) return launch_codes(code_bytes, cat, a, smem, 1, nullptr, ctas);
-  if (layout == 0 && top) {
+  const bool pay = layout == 3;
+  if ((layout == 0 || pay) && top) {
     static TopRecords none{};
-    return launch_complete_top(planes, cat, a, none, smem, 1, nullptr, ctas);
+    return launch_complete_top(planes, cat, pay, a, none, smem, 1, nullptr, ctas);
   }
-  return layout == 0 ? launch_complete(planes, cat, a, smem, 1, nullptr, ctas)
-                     : launch_explicit(planes, cat, a, smem, 1, nullptr, ctas);
+  return (layout == 0 || pay) ? launch_complete(planes, cat, pay, a, smem, 1, nullptr, ctas)
+                              : launch_explicit(planes, cat, a, smem, 1, nullptr, ctas);
 }
 
 cudaError_t launch_transpose(const float* in, long long rows, int F, float* out, long long ld,

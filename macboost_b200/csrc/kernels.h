@@ -89,7 +89,8 @@ struct TopRecords {
 };
 
 // Launch the forest kernel on `stream`.  layout: 0 complete, 1 explicit,
-// 2 complete with binned codes (code_bytes 1 or 2); planes: NaN planes in the
+// 2 complete with binned codes (code_bytes 1 or 2), 3 complete with the
+// default direction in the record word (FlatForest::payload); planes: NaN planes in the
 // tile; cat: the model has categorical splits; top (complete layout only):
 // the first two levels' records, or null to read every level from shared memory.
 cudaError_t launch_forest(int layout, bool planes, bool cat, const KArgs& a, size_t smem,

@@ -225,8 +225,10 @@ __device__ __forceinline__ void issue_block(const KArgs& a, int b, uint32_t dst,
 // slot of their default direction and compare unordered; otherwise bit0 of
 // the record selects the ordered compare for default-left, unless NONAN (a
 // tile without NaN) makes both compares equal.  CAT: categorical records
-// (bit1) test the node's mask at the value's code.
-template <bool PLANES, bool CAT, bool NONAN = false>
+// (bit1) test the node's mask at the value's code.  PAY (no planes, no
+// categorical splits): the record word itself is the fmax operand below
+// (kRecPayloadLeft/Right), one instruction less per node than the shift.
+template <bool PLANES, bool CAT, bool NONAN = false, bool PAY = false>
 __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsigned* masks,
                                           int data_bins) {
   const uint32_t addr = rowbase + ((PLANES && !CAT) ? r.x : (r.x & kRecSlotMask));
@@ -268,6 +270,11 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
   // (slot offsets are multiples of 128 bytes), and the funnel shift takes its
   // count modulo 32, so the record word itself is the shift count.
   static_assert(kRecDefaultLeft == 1u && (kRecSlotMask & 31u) == 0u, "record layout");
+  // PAY: r.x is a NaN (default right: fmax keeps v) or a float at or below
+  // -2^127 that no default-left threshold lies under (fmax turns NaN into a
+  // value left of the threshold; a value below it is left either way).
+  static_assert(!PAY || (!PLANES && !CAT), "payload records: complete layout, no planes");
+  if constexpr (PAY) return uint32_t(!(fmaxf(v, __uint_as_float(r.x)) <= t));
   const float c = __uint_as_float(__funnelshift_l(0u, 0x7FC00000u, r.x));
   return uint32_t(!(fmaxf(v, c) <= t));
 }
@@ -775,10 +782,11 @@ __device__ __forceinline__ void run_rows(const KArgs& a, unsigned char* smem, Sc
 // Per-layout launchers (kernels_complete.cu, kernels_explicit.cu, kernels_codes.cu).
 cudaError_t launch_codes(int code_bytes, bool cat, const KArgs& a, size_t smem, int grid,
                          cudaStream_t stream, int* occupancy_out);
-cudaError_t launch_complete_top(bool planes, bool cat, const KArgs& a, const TopRecords& top,
-                                size_t smem, int grid, cudaStream_t stream, int* occupancy_out);
-cudaError_t launch_complete(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
-                            cudaStream_t stream, int* occupancy_out);
+cudaError_t launch_complete_top(bool planes, bool cat, bool pay, const KArgs& a,
+                                const TopRecords& top, size_t smem, int grid,
+                                cudaStream_t stream, int* occupancy_out);
+cudaError_t launch_complete(bool planes, bool cat, bool pay, const KArgs& a, size_t smem,
+                            int grid, cudaStream_t stream, int* occupancy_out);
 cudaError_t launch_explicit(bool planes, bool cat, const KArgs& a, size_t smem, int grid,
                             cudaStream_t stream, int* occupancy_out);
 

@@ -50,8 +50,10 @@ struct NoTop {};
 // levels 0 and 1 come from the kernel parameter: the root record is warp
 // uniform, and both level-1 records are loaded (uniform) and selected, so a
 // tree's first two levels cost no shared-memory wavefront; the walk then
-// resumes at heap node 3 + 2 r0 + r1 (slot 4 + 2 r0 + r1).
-template <int KT, int G, bool PLANES, bool CAT, int DC, class Top>
+// resumes at heap node 3 + 2 r0 + r1 (slot 4 + 2 r0 + r1).  PAY (no planes,
+// no categorical splits): numeric records carry their default direction as
+// the fmax operand itself (dev::route).
+template <int KT, int G, bool PLANES, bool CAT, int DC, bool PAY, class Top>
 __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* smem, const Top& top) {
   constexpr bool kTop = !std::is_same<Top, NoTop>::value;
   const int D = DC > 0 ? DC : a.D;  // DC: depth fixed at compile time, 0 = from a.D
@@ -74,12 +76,12 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
 #pragma unroll
         for (int j = 0; j < G; ++j) {
           const unsigned long long q0 = top.rec[t0 + 3 * j];
-          const uint32_t r0 = dev::route<PLANES, CAT, NN>(make_uint2(unsigned(q0), unsigned(q0 >> 32)),
+          const uint32_t r0 = dev::route<PLANES, CAT, NN, PAY>(make_uint2(unsigned(q0), unsigned(q0 >> 32)),
                                                        rowbase, a.masks, a.data_bins);
           const unsigned long long q1 = top.rec[t0 + 3 * j + 1];
           const unsigned long long q2 = top.rec[t0 + 3 * j + 2];
           const unsigned long long q = r0 ? q2 : q1;
-          const uint32_t r1 = dev::route<PLANES, CAT, NN>(make_uint2(unsigned(q), unsigned(q >> 32)),
+          const uint32_t r1 = dev::route<PLANES, CAT, NN, PAY>(make_uint2(unsigned(q), unsigned(q >> 32)),
                                                        rowbase, a.masks, a.data_bins);
           o[j] = A[j] + 8u * (4u + 2u * r0 + r1);
         }
@@ -90,7 +92,7 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
         for (int j = 0; j < G; ++j) r[j] = dev::lds_v2(o[j]);
 #pragma unroll
         for (int j = 0; j < G; ++j) {
-          const uint32_t right = dev::route<PLANES, CAT, NN>(r[j], rowbase, a.masks, a.data_bins);
+          const uint32_t right = dev::route<PLANES, CAT, NN, PAY>(r[j], rowbase, a.masks, a.data_bins);
           o[j] = 2u * o[j] - A[j] + (right << 3);
         }
       }
@@ -120,27 +122,27 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
   dev::run_rows<KT, !PLANES>(a, smem, score);
 }
 
-template <int KT, int G, bool PLANES, bool CAT, int DC = 0>
+template <int KT, int G, bool PLANES, bool CAT, int DC = 0, bool PAY = false>
 __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_complete_kernel(const KArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  complete_tiles<KT, G, PLANES, CAT, DC>(a, smem, NoTop{});
+  complete_tiles<KT, G, PLANES, CAT, DC, PAY>(a, smem, NoTop{});
 }
 
-template <int KT, int G, bool PLANES, bool CAT, int DC = 0>
+template <int KT, int G, bool PLANES, bool CAT, int DC = 0, bool PAY = false>
 __global__ void __launch_bounds__(dev::Bounds<KT, G>::kMaxThreads, 1)
     forest_complete_top_kernel(const KArgs a, const TopRecords top) {
   extern __shared__ __align__(128) unsigned char smem[];
-  complete_tiles<KT, G, PLANES, CAT, DC>(a, smem, top);
+  complete_tiles<KT, G, PLANES, CAT, DC, PAY>(a, smem, top);
 }
 
 using KernelFn = void (*)(const KArgs);
 using TopKernelFn = void (*)(const KArgs, const TopRecords);
 
 // Fixed-depth builds (kernels_complete_fixed.cu): the kernel for (planes,
-// cat, K, G, D), or null where only the run-time-depth build exists.
-KernelFn pick_fixed(bool planes, bool cat, int K, int G, int D);
-TopKernelFn pick_top_fixed(bool planes, bool cat, int K, int G, int D);
+// cat, pay, K, G, D), or null where only the run-time-depth build exists.
+KernelFn pick_fixed(bool planes, bool cat, bool pay, int K, int G, int D);
+TopKernelFn pick_top_fixed(bool planes, bool cat, bool pay, int K, int G, int D);
 
 }  // namespace complete
 }  // namespace mb

@@ -13,47 +13,49 @@ namespace complete {
 namespace {
 
 template <int KT, int G, int D>
-KernelFn fixed(bool planes, bool cat) {
+KernelFn fixed(bool planes, bool cat, bool pay) {
   if (planes)
     return cat ? forest_complete_kernel<KT, G, true, true, D>
                : forest_complete_kernel<KT, G, true, false, D>;
-  return cat ? forest_complete_kernel<KT, G, false, true, D>
+  if (cat) return forest_complete_kernel<KT, G, false, true, D>;
+  return pay ? forest_complete_kernel<KT, G, false, false, D, true>
              : forest_complete_kernel<KT, G, false, false, D>;
 }
 
 template <int KT, int G, int D>
-TopKernelFn fixed_top(bool planes, bool cat) {
+TopKernelFn fixed_top(bool planes, bool cat, bool pay) {
   if (planes)
     return cat ? forest_complete_top_kernel<KT, G, true, true, D>
                : forest_complete_top_kernel<KT, G, true, false, D>;
-  return cat ? forest_complete_top_kernel<KT, G, false, true, D>
+  if (cat) return forest_complete_top_kernel<KT, G, false, true, D>;
+  return pay ? forest_complete_top_kernel<KT, G, false, false, D, true>
              : forest_complete_top_kernel<KT, G, false, false, D>;
 }
 
 }  // namespace
 
-KernelFn pick_fixed(bool planes, bool cat, int K, int G, int D) {
-  if (K == 10 && G == 10 && D == 6) return fixed<10, 10, 6>(planes, cat);
+KernelFn pick_fixed(bool planes, bool cat, bool pay, int K, int G, int D) {
+  if (K == 10 && G == 10 && D == 6) return fixed<10, 10, 6>(planes, cat, pay);
   if (K != 1 || G != 8) return nullptr;
   switch (D) {
-    case 4: return fixed<1, 8, 4>(planes, cat);
-    case 5: return fixed<1, 8, 5>(planes, cat);
-    case 6: return fixed<1, 8, 6>(planes, cat);
-    case 7: return fixed<1, 8, 7>(planes, cat);
-    case 8: return fixed<1, 8, 8>(planes, cat);
+    case 4: return fixed<1, 8, 4>(planes, cat, pay);
+    case 5: return fixed<1, 8, 5>(planes, cat, pay);
+    case 6: return fixed<1, 8, 6>(planes, cat, pay);
+    case 7: return fixed<1, 8, 7>(planes, cat, pay);
+    case 8: return fixed<1, 8, 8>(planes, cat, pay);
     default: return nullptr;
   }
 }
 
-TopKernelFn pick_top_fixed(bool planes, bool cat, int K, int G, int D) {
-  if (K == 10 && G == 10 && D == 6) return fixed_top<10, 10, 6>(planes, cat);
+TopKernelFn pick_top_fixed(bool planes, bool cat, bool pay, int K, int G, int D) {
+  if (K == 10 && G == 10 && D == 6) return fixed_top<10, 10, 6>(planes, cat, pay);
   if (K != 1 || G != 8) return nullptr;
   switch (D) {
-    case 4: return fixed_top<1, 8, 4>(planes, cat);
-    case 5: return fixed_top<1, 8, 5>(planes, cat);
-    case 6: return fixed_top<1, 8, 6>(planes, cat);
-    case 7: return fixed_top<1, 8, 7>(planes, cat);
-    case 8: return fixed_top<1, 8, 8>(planes, cat);
+    case 4: return fixed_top<1, 8, 4>(planes, cat, pay);
+    case 5: return fixed_top<1, 8, 5>(planes, cat, pay);
+    case 6: return fixed_top<1, 8, 6>(planes, cat, pay);
+    case 7: return fixed_top<1, 8, 7>(planes, cat, pay);
+    case 8: return fixed_top<1, 8, 8>(planes, cat, pay);
     default: return nullptr;
   }
 }

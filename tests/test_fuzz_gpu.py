@@ -22,7 +22,7 @@ from macboost_b200 import synth
 pytestmark = pytest.mark.gpu
 
 PLANS = ["", "codes=0", "codes=0,planes=0", "codes=1", "codes=0,top=1",
-         "codes=0,planes=0,top=1"]
+         "codes=0,planes=0,top=1", "codes=0,planes=0,pay=0"]
 SPECIAL = np.float32([0.0, -0.0, 1e-40, -1e-40, 3e38, -3e38, 0.5, -0.5, 1.0])
 
 

@@ -216,11 +216,13 @@ def _cudart():
 
 
 @pytest.mark.parametrize("plan", ["codes=0", "codes=0,planes=0", "codes=1", "codes=1,G=8",
-                                  "codes=0,top=1", "codes=0,planes=0,top=1", "codes=0,top=0"])
+                                  "codes=0,top=1", "codes=0,planes=0,top=1", "codes=0,top=0",
+                                  "codes=0,planes=0,pay=0", "codes=0,planes=0,top=1,pay=0"])
 @pytest.mark.parametrize("cfg", ["cfg1", "cfg2", "cfg3", "cfg4"])
 def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
     """Each kernel family (fp32 tiles with NaN planes, fp32 with default-left
-    flags, binned codes; the first two levels from shared memory or from the
+    flags, the default direction as the record word or by a shift of its flag
+    bit, binned codes; the first two levels from shared memory or from the
     kernel parameter), forced through MACBOOST_PLAN, against the oracle."""
     core = gpu
     if cfg == "cfg4" and "G=8" in plan:
@@ -237,6 +239,10 @@ def test_every_layout_vs_oracle(gpu, oracle_built, cfg, plan, monkeypatch):
         assert desc["top_params"] is True
     if "top=0" in plan:
         assert desc["top_params"] is False
+    if "pay=0" in plan:
+        assert desc["payload_records"] is False
+    elif "planes=0" in plan and desc["layout"] == "complete" and cfg != "cfg3":
+        assert desc["payload_records"] is True   # no categorical splits, no planes
     om = O.model_from_dict(json.loads(text))
     X = synth.make_data(cfg, rows=5003, row_start=999, layout="row")
     raw_o, leaf_o = O.predict_raw(om, X, want_leaf=True)

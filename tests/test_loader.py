@@ -219,3 +219,32 @@ def test_plan_restrictions_from_the_environment(lib_built, monkeypatch):
     d = json.loads(core.describe(core.load_json(text)))
     assert d["grid_cap"] == 3 and d["chunk_rows"] == 4096 and d["claim"] is False
     assert d["tile_buffers"] == 2
+
+
+def test_payload_records_choice(lib_built, monkeypatch):
+    """Without NaN planes or categorical splits, complete-layout records carry
+    the default direction as the walk's fmax operand, a float at or below
+    -2^127 for default-left nodes; a forest with a default-left threshold below
+    -2^127 would have values under it and keeps the shifted-flag route."""
+    core = lib_built
+    monkeypatch.setenv("MACBOOST_PLAN", "planes=0,codes=0")
+
+    def describe(threshold, default_left):
+        rng = np.random.default_rng(11)
+        tl = [synth._complete_tree(rng, 4, 6, synth.EDGES_256, 0.1) for _ in range(8)]
+        tl[3]["threshold"][2] = np.float32(threshold)
+        tl[3]["flags"][2] = default_left
+        m = {"version": 1, "objective": 0, "numBins": 256, "baseScore": 0.0,
+             "numFeatures": 6, "categorical": [], "trees": tl, "numClasses": 1,
+             "baseScores": [0.0]}
+        d = json.loads(core.describe(core.load_json(synth.model_to_json(m))))
+        assert d["layout"] == "complete" and d["nan_planes"] is False
+        return d["payload_records"]
+
+    assert describe(0.5, 1) is True
+    assert describe(-1.7e38, 1) is True          # above -2^127 = -1.7014118e38
+    assert describe(-1.71e38, 0) is True         # default right: the operand is a NaN
+    assert describe(-1.71e38, 1) is False
+    assert describe(-3.4e38, 1) is False
+    monkeypatch.setenv("MACBOOST_PLAN", "planes=0,codes=0,pay=0")
+    assert describe(0.5, 1) is False
