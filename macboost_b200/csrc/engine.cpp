@@ -116,7 +116,6 @@ KArgs make_args(const Engine& e, const DeviceState& d, int kind) {
   a.block_rec_base = d.block_rec_base;
   a.masks = d.masks;
   a.leaf_heap = d.leaf_heap;
-  a.leaf_identity = f.heap_identity && !f.codes && f.layout == Layout::kComplete;
   a.base = d.base;
   a.S_stage = f.S_stage;
   a.conv_src = d.conv_src;

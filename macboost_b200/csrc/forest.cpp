@@ -528,15 +528,6 @@ static bool flatten_f32(const Model& m, FlatForest& f, std::string& err, int for
       fill(0, 0, -1, 0);
       f.nodes += int64_t(NL) * 2 - 1;
     }
-    // Trees of exactly depth D in heap order (no padding) number their leaves
-    // 2^D - 1 + l: the kernel then computes a leaf index instead of reading it.
-    f.heap_identity = true;
-    for (int t = 0; t < f.T && f.heap_identity; ++t)
-      for (int l = 0; l < NL; ++l)
-        if (f.leaf_heap[size_t(t) * NL + size_t(l)] != NL - 1 + l) {
-          f.heap_identity = false;
-          break;
-        }
     // Heap nodes 0, 1, 2 (slots 1, 2, 3) of every tree for the kernel
     // parameter.  It removes the first two levels' shared-memory record loads,
     // which pays where those loads bound the walk: with NaN planes (one compare
@@ -658,7 +649,6 @@ std::string describe_forest(const FlatForest& f) {
   s += ",\"codes\":" + std::string(f.codes ? "true" : "false");
   s += ",\"top_params\":" + std::string(f.top_recs.empty() ? "false" : "true");
   s += ",\"payload_records\":" + std::string(f.payload ? "true" : "false");
-  s += ",\"leaf_identity\":" + std::string(f.heap_identity && !f.codes ? "true" : "false");
   if (f.layout == Layout::kExplicit)
     s += ",\"compact_children\":" + std::string(f.compact_children ? "true" : "false");
   if (f.codes) {

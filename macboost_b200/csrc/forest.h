@@ -144,7 +144,6 @@ struct FlatForest {
   std::vector<uint64_t> block_off;     // [nblocks + 1] byte offsets in blob
   std::vector<uint32_t> full_masks;    // [n][8]
   std::vector<int32_t> leaf_heap;      // complete: [Tpad][2^D]; explicit: [records]
-  bool heap_identity = false;          // complete: leaf_heap[t][l] == 2^D - 1 + l for t < T
   std::vector<uint32_t> block_rec_base;// explicit: first record index of each block
   int D = 0;                           // complete layout depth
   uint32_t leaf_off = 0;               // complete layout: leaves offset in a block

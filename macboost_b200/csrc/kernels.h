@@ -39,7 +39,6 @@ struct KArgs {
   const unsigned* block_rec_base;       // explicit layout: first record index per block
   const unsigned* masks;                // full categorical masks, 8 words each
   const int* leaf_heap;
-  int leaf_identity;               // complete layout: leaf_heap[t][l] is 2^D - 1 + l (not read)
   const float* base;                    // [K] starting margins
   int K, G, T, D, Tb, nblocks;      // G: trees walked at once per thread
   // Binned-code layout: per staged slot {search table, NaN-right code byte

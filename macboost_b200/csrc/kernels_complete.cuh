@@ -108,9 +108,7 @@ __device__ __forceinline__ void complete_tiles(const KArgs& a, unsigned char* sm
 #pragma unroll
         for (int j = 0; j < G; ++j) {
           const uint32_t leaf = (o[j] - A[j]) / 8u - NL;
-          li[j] = t0 + j >= a.T ? 0
-                  : a.leaf_identity ? int(NL - 1u + leaf)
-                                    : __ldg(a.leaf_heap + size_t(t0 + j) * NL + leaf);
+          li[j] = t0 + j < a.T ? __ldg(a.leaf_heap + size_t(t0 + j) * NL + leaf) : 0;
         }
         dev::store_leaf_run<G>(a.out_leaf + row * a.T + t0, li, a.T - t0);
       }

@@ -248,20 +248,3 @@ def test_payload_records_choice(lib_built, monkeypatch):
     assert describe(-3.4e38, 1) is False
     monkeypatch.setenv("MACBOOST_PLAN", "planes=0,codes=0,pay=0")
     assert describe(0.5, 1) is False
-
-
-def test_leaf_identity_choice(lib_built):
-    """Leaf indices of trees of exactly the forest's depth are computed from
-    the walk's final position; a shallower (padded) tree makes the kernel read
-    them from the leaf table."""
-    core = lib_built
-    rng = np.random.default_rng(12)
-    tl = [synth._complete_tree(rng, 5, 6, synth.EDGES_256, 0.1) for _ in range(8)]
-    base = {"version": 1, "objective": 0, "numBins": 256, "baseScore": 0.0, "numFeatures": 6,
-            "categorical": [], "numClasses": 1, "baseScores": [0.0]}
-    d = json.loads(core.describe(core.load_json(synth.model_to_json({**base, "trees": tl}))))
-    assert d["layout"] == "complete" and d["leaf_identity"] is True
-    shallow = tl + [synth._complete_tree(rng, 3, 6, synth.EDGES_256, 0.1)]
-    d = json.loads(core.describe(core.load_json(synth.model_to_json({**base, "trees": shallow}))))
-    assert d["layout"] == "complete" and d["leaf_identity"] is False
-
