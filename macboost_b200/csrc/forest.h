@@ -80,7 +80,7 @@ constexpr int kRecChildShift = 18;
 // compare sends NaN right), a finite value at or below -2^127 for default-left
 // ones (fmax turns NaN into it) -- with the slot offset in bits 7..17.
 constexpr uint32_t kRecPayloadLeft = 0xFF000000u;
-constexpr uint32_t kRecPayloadRight = 0xFF800001u;
+constexpr uint32_t kRecPayloadRight = 0xFFC00000u;  // a quiet NaN
 constexpr uint32_t kMaxChildDelta = 16383u;
 constexpr uint32_t kMaxCompactDelta = 2047u;  // 8 x distance still fits bits 18-31
 
