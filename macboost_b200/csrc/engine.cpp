@@ -67,7 +67,8 @@ int ensure(void*& buf, size_t& cap, size_t bytes, std::string& err) {
   return 0;
 }
 
-// Kernel family: 0 complete, 1 explicit, 2 complete with binned codes.
+// Kernel family: 0 complete, 1 explicit, 2 complete with binned codes, 3 complete
+// with the default direction carried as the record word (FlatForest::payload).
 int layout_code(const FlatForest& f) { return f.codes ? 2 : (f.payload ? 3 : int(f.layout)); }
 
 // Device-wait settings, read at each launch: MACBOOST_WAIT_LIMIT_US bounds

@@ -273,7 +273,7 @@ __device__ __forceinline__ uint32_t route(uint2 r, uint32_t rowbase, const unsig
   // PAY: r.x is a NaN (default right: fmax keeps v) or a float at or below
   // -2^127 that no default-left threshold lies under (fmax turns NaN into a
   // value left of the threshold; a value below it is left either way).
-  static_assert(!PAY || (!PLANES && !CAT), "payload records: complete layout, no planes");
+  static_assert(!PAY || (!PLANES && !CAT), "payload records: no planes, no categorical splits");
   if constexpr (PAY) return uint32_t(!(fmaxf(v, __uint_as_float(r.x)) <= t));
   const float c = __uint_as_float(__funnelshift_l(0u, 0x7FC00000u, r.x));
   return uint32_t(!(fmaxf(v, c) <= t));
